@@ -1,0 +1,510 @@
+#!/usr/bin/env python
+"""Benchmark of the WANferenz MoE decode layer on B200.
+
+Workload: DeepSeek-V4-Flash-shaped MoE layer (hidden 4096, 256 routed FP4
+experts x inter 2048, 1 FP8 shared expert, top-6 sigmoid routing, route scale
+1.5), random-init weights from the reference's fixture recipe (N(0, 0.02) ->
+FP4 E2M1 + UE8M0 per 32; shared FP8 E4M3 per 128x128), synthetic N(0, 1) bf16
+tokens.  One step = one layer forward over one batch of ``--tokens`` tokens
+per GPU.  ``--layers`` distinct layers are cycled so each step's weights are
+cold in L2 (8 layers x ~27 MB of router + shared weights alone > 126 MB L2);
+no L2 flush is used.
+
+N > 1 (torchrun, one rank per GPU): expert parallel, each rank holds 256/N
+experts and its own ``--tokens`` tokens (weak scaling); token batches are
+all-gathered over NCCL, every rank computes its local experts' partial sums
+for the gathered batch, and a reduce-scatter returns each rank its tokens'
+sums (the reference's all-reduce, architecture.py:791-792, restricted to the
+owner's rows).
+
+``--impl reference`` times the reference algorithm on the host cores: the
+numpy oracle port (the reference itself is Python/TileLang and is not
+installed on the GPU box).
+
+Prints ONE JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, I, E, K_TOP = 4096, 2048, 256, 6
+FP4_EXPERT_BYTES = 3 * I * D // 2 + 3 * I * D // 32      # w1, w3, w2 + scales = 13,369,344
+SHARED_BYTES = 3 * I * D + 3 * (I // 128) * (D // 128)    # 25,166,592 (+ e8m0 scales)
+ROUTER_BYTES = E * D * 2 + E * 4
+METRIC = "MoE layer tokens/s (V4-Flash decode layer: hidden 4096, 256 FP4 experts x 2048, top-6, FP8 shared)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--tokens", type=int, default=16, help="tokens per GPU per step")
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--sweep", default="1,4,16", help="extra token counts measured at N=1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic layers (GPU-side generation with the reference's fixture recipe)
+# ---------------------------------------------------------------------------
+def fp8_block_quant_torch(w):
+    """fp4_grouped._fp8_block_quant (fp4_grouped.py:354-365) in torch on the GPU (fixture only)."""
+    import torch
+
+    n, k = w.shape
+    b = w.float().unflatten(0, (n // 128, 128)).unflatten(-1, (k // 128, 128))
+    amax = b.abs().amax(dim=(1, 3)).clamp_min(1e-4)
+    scale = torch.pow(2.0, torch.ceil(torch.log2(amax / 448.0)))
+    q = (b / scale[:, None, :, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.reshape(n, k).view(torch.uint8), scale.to(torch.float8_e8m0fnu).view(torch.uint8)
+
+
+def make_layer(seed, rank, world, max_tokens, device):
+    import torch
+
+    from wanferenz_b200 import ops
+    from wanferenz_b200.moe import MoELayer, MoEWeights
+
+    El = E // world
+    e0 = rank * El
+    g = torch.Generator(device=device)
+    g.manual_seed(1000 + seed)  # router + shared: identical on every rank
+    gate_w = (torch.randn(E, D, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    gate_b = torch.randn(E, device=device, generator=g) * 0.01
+    sh = [(torch.randn(*shp, device=device, generator=g) * 0.02).to(torch.bfloat16)
+          for shp in ((I, D), (I, D), (D, I))]
+    q = [fp8_block_quant_torch(t) for t in sh]
+    w13 = torch.empty(El, 2 * I, D // 2, dtype=torch.uint8, device=device)
+    w13_s = torch.empty(El, 2 * I, D // 32, dtype=torch.uint8, device=device)
+    w2 = torch.empty(El, D, I // 2, dtype=torch.uint8, device=device)
+    w2_s = torch.empty(El, D, I // 32, dtype=torch.uint8, device=device)
+    for e in range(e0, e0 + El):
+        g.manual_seed(1000003 * (seed + 1) + e)
+        a = (torch.randn(2 * I, D, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        wq, ws = ops.fp4_act_quant(a)
+        w13[e - e0].copy_(wq.view(torch.uint8)); w13_s[e - e0].copy_(ws.view(torch.uint8))
+        b = (torch.randn(D, I, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        wq, ws = ops.fp4_act_quant(b)
+        w2[e - e0].copy_(wq.view(torch.uint8)); w2_s[e - e0].copy_(ws.view(torch.uint8))
+    weights = MoEWeights(gate_w=gate_w, gate_b=gate_b, tid2eid=None, w13=w13, w13_s=w13_s, w2=w2,
+                         w2_s=w2_s, shared_w13=torch.cat([q[0][0], q[1][0]]),
+                         shared_s13=torch.cat([q[0][1], q[1][1]]), shared_w2=q[2][0],
+                         shared_s2=q[2][1])
+    return MoELayer(weights, dim=D, inter_dim=I, n_experts=E, topk=K_TOP, score_func="sigmoid",
+                    route_scale=1.5, n_local_experts=El, expert_offset=e0, max_tokens=max_tokens)
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes per kernel for one step, from the step's routing
+# ---------------------------------------------------------------------------
+def step_bytes(indices, T, e0, El):
+    """Bytes each kernel must move at minimum, given this step's expert indices [T, k]."""
+    import numpy as np
+
+    idx = np.asarray(indices)
+    local = idx[(idx >= e0) & (idx < e0 + El)]
+    n_exp = len(np.unique(local))
+    pairs = sum(len(set(r[(r >= e0) & (r < e0 + El)].tolist())) for r in idx)
+    w13 = 2 * I * (D // 2 + D // 32)
+    w2 = D * (I // 2 + I // 32)
+    k1 = ROUTER_BYTES + 2 * I * D + 2 * (I // 128) * (D // 128) + T * D * 2 + T * I * 2
+    k2 = n_exp * w13 + D * I + (D // 128) * (I // 128) + T * D * 2 + pairs * I * 2 + T * I * 2 + T * D * 2
+    k3 = n_exp * w2 + pairs * I * 2 + pairs * D * 2 * 2 + T * D * 2 * 2
+    return {"k_moe_up": k1, "k_moe_mid": k2, "k_moe_down": k3, "experts": n_exp, "pairs": pairs}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu(args):
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from wanferenz_b200 import _lib as L
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    T = args.tokens
+    Tg = T * world
+    layers = [make_layer(s, rank, world, max(Tg, 16), dev) for s in range(args.layers)]
+    lib = L.load()
+    hbm, peak_kind = peaks()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def measure(Tloc, K, W, graph=True):
+        """K graph-captured steps; returns per-step times and per-kernel event times."""
+        n = K + W
+        xs = [torch.randn(Tloc, D, device=dev).to(torch.bfloat16) for _ in range(n)]
+        ys = [torch.empty(Tloc, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
+        idx = [torch.empty(Tloc * world, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+        Tgl = Tloc * world
+        xg = [torch.empty(Tgl, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
+        part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]
+        mine = [torch.empty(Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
+
+        def one(i):
+            lay = layers[i % len(layers)]
+            st = L.stream_ptr()
+            ev = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in evs[i]])
+            if world == 1:
+                rc = lib.wf_moe_forward_timed(ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct),
+                                              L.ptr(xs[i]), 0, Tloc, L.ptr(ys[i]), 0, 0, L.ptr(idx[i]),
+                                              L.ptr(lay.workspace), lay.workspace.numel(), st, ev)
+                L.check(rc, "wf_moe_forward_timed")
+            else:
+                dist.all_gather_into_tensor(xg[i], xs[i])
+                rc = lib.wf_moe_forward_timed(ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct),
+                                              L.ptr(xg[i]), 0, Tgl, 0, L.ptr(part[i]), 0, L.ptr(idx[i]),
+                                              L.ptr(lay.workspace), lay.workspace.numel(), st, ev)
+                L.check(rc, "wf_moe_forward_timed")
+                dist.reduce_scatter_tensor(mine[i], part[i])
+                # shared expert output of this rank's rows + bf16 cast (architecture.py:793-794)
+                L.check(lib.wf_moe_finish(ctypes.byref(lay.cfg), L.ptr(mine[i]), Tloc, rank * Tloc,
+                                          L.ptr(ys[i]), L.ptr(lay.workspace), lay.workspace.numel(), st),
+                        "wf_moe_finish")
+
+        for i in range(W):
+            one(i)
+        torch.cuda.synchronize()
+        g = None
+        if graph and world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(W, n):
+                    one(i)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            t0.record()
+            if g is not None:
+                g.replay()
+            else:
+                for i in range(W, n):
+                    one(i)
+            t1.record()
+            torch.cuda.synchronize()
+        barrier()
+        total_ms = t0.elapsed_time(t1)
+        kern = {"k_moe_up": [], "k_moe_mid": [], "k_moe_down": []}
+        for i in range(W, n):
+            e = evs[i]
+            kern["k_moe_up"].append(e[0].elapsed_time(e[1]))
+            kern["k_moe_mid"].append(e[1].elapsed_time(e[2]))
+            kern["k_moe_down"].append(e[2].elapsed_time(e[3]))
+        routing = [idx[i].cpu().numpy() for i in range(W, n)]
+        del g
+        return total_ms, kern, routing, clk.summary()
+
+    def stats(Tloc, K, W):
+        total_ms, kern, routing, clk = measure(Tloc, K, W)
+        t = torch.tensor([total_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        ms = total_ms / K
+        lay0 = layers[0]
+        byts = [step_bytes(r, Tloc * world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
+        mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
+        kms = {k: float(np.mean(v)) for k, v in kern.items()}
+        layer_bytes = mean["k_moe_up"] + mean["k_moe_mid"] + mean["k_moe_down"]
+        return dict(ms=ms, total_ms=total_ms, kms=kms, bytes=mean, layer_bytes=layer_bytes, clocks=clk)
+
+    main = stats(T, args.steps, args.warmup)
+    sweep = {}
+    if world == 1:
+        for s in [int(v) for v in args.sweep.split(",") if v]:
+            if s == T:
+                r = main
+            else:
+                r = stats(s, args.steps, args.warmup)
+            layer_gbs = r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9
+            sweep[f"T{s}"] = {
+                "us_per_step": round(r["ms"] * 1e3, 2), "tokens_per_s": round(s / (r["ms"] * 1e-3), 1),
+                "layer_GBps": round(layer_gbs, 1), "layer_frac_of_measured_hbm": round(layer_gbs / hbm, 3),
+                "experts_touched": round(r["bytes"]["experts"], 1),
+                "kernel_us": {k: round(v * 1e3, 2) for k, v in r["kms"].items()},
+            }
+    # dominant kernel roofline
+    kms = main["kms"]
+    dom = max(kms, key=kms.get)
+    ach = main["bytes"][dom] / (kms[dom] * 1e-3) / 1e9
+    value = T * world / (main["ms"] * 1e-3)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(layers, T, args.steps, args.warmup, dev, world, rank)
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32",
+        "data": "synthetic (seeded N(0,0.02) weights quantized like the reference fixtures; N(0,1) bf16 tokens)",
+        "config": {
+            "workload": f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing",
+            "tokens_per_gpu": T, "global_tokens": T * world, "hidden": D, "experts": E, "inter": I,
+            "topk": K_TOP, "layers_cycled": args.layers, "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": f"{args.layers} distinct layers cycled (per-step weights cold in L2), no flush",
+            "timing": "CUDA graph of K steps, CUDA events on the launching stream" if world == 1 else
+                      "eager steps (NCCL), CUDA events, max over ranks",
+            "us_per_step": round(main["ms"] * 1e3, 2),
+            "layer_GBps": round(main["layer_bytes"] / (main["ms"] * 1e-3) / 1e9, 1),
+            "kernel_us": {k: round(v * 1e3, 2) for k, v in kms.items()},
+            "experts_touched_per_rank": round(main["bytes"]["experts"], 1),
+            "sweep": sweep,
+        },
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / hbm, 4),
+                     "traffic": None, "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
+        "clocks": main["clocks"],
+        "gpu_launches": 3 * args.steps * (2 if world > 1 else 1) - (args.steps if world > 1 else 0),
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(T)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def run_e2e(layers, T, K, W, dev, world, rank):
+    """Public API (MoELayer.forward), host pinned input -> device -> host output every step."""
+    import torch
+    import torch.distributed as dist
+
+    n = K + W
+    xh = [torch.randn(T, D).to(torch.bfloat16).pin_memory() for _ in range(n)]
+    yh = [torch.empty(T, D, dtype=torch.bfloat16).pin_memory() for _ in range(n)]
+    xd = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+
+    def one(i):
+        lay = layers[i % len(layers)]
+        xd.copy_(xh[i], non_blocking=True)
+        if world == 1:
+            y = lay.forward(xd)
+        else:
+            from wanferenz_b200.ep import ep_forward
+            y = ep_forward(lay, xd)
+        yh[i].copy_(y, non_blocking=True)
+
+    for i in range(W):
+        one(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(W, n):
+        one(i)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item()) / K
+    return {"value": round(T * world / (ms * 1e-3), 1), "unit": "tokens/s",
+            "us_per_step": round(ms * 1e3, 2), "h2d_bytes_per_step": T * D * 2,
+            "d2h_bytes_per_step": T * D * 2, "api": "wanferenz_b200.moe.MoELayer.forward"}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle port of the reference's torch CPU path
+# ---------------------------------------------------------------------------
+def cpu_layer(seed=0):
+    """Oracle-side layer with the config-2 shapes; expert bytes random (cost does not depend on values)."""
+    import numpy as np
+
+    from oracle import fixtures as F
+
+    spec = F.CONFIG2
+    syn = F.SyntheticLayer(F.LayerSpec(**{**spec.as_dict(), "seed": seed}))
+    cache = {}
+    r = np.random.default_rng(seed)
+
+    def expert(e):
+        if e not in cache:
+            cache[e] = (r.integers(0, 256, (I, D // 2), dtype=np.uint8),
+                        r.integers(118, 125, (I, D // 32), dtype=np.uint8),
+                        r.integers(0, 256, (I, D // 2), dtype=np.uint8),
+                        r.integers(118, 125, (I, D // 32), dtype=np.uint8),
+                        r.integers(0, 256, (D, I // 2), dtype=np.uint8),
+                        r.integers(118, 125, (D, I // 32), dtype=np.uint8))
+        return cache[e]
+
+    sh = (r.integers(0, 126, (I, D), dtype=np.uint8), r.integers(118, 125, (I // 128, D // 128), dtype=np.uint8),
+          r.integers(0, 126, (I, D), dtype=np.uint8), r.integers(118, 125, (I // 128, D // 128), dtype=np.uint8),
+          r.integers(0, 126, (D, I), dtype=np.uint8), r.integers(118, 125, (D // 128, I // 128), dtype=np.uint8))
+    params = syn.params()
+    params["experts"] = expert
+    params["shared"] = sh
+    return syn, params
+
+
+def cpu_forward_time(T, reps=1, seed=0):
+    import numpy as np
+
+    from oracle import moe_oracle as O
+
+    syn, params = cpu_layer(seed)
+    times = []
+    for rep in range(reps):
+        x16, _ = syn.activations(T, draw=100 + rep)
+        x = O.bf16_to_f32(x16)
+        t = time.perf_counter()
+        O.moe_forward(x, params, acc=np.float32)
+        times.append(time.perf_counter() - t)
+    return times
+
+
+def cpu_baseline(T):
+    t = cpu_forward_time(T, reps=1)
+    s = float(np.median(t)) if (np := __import__("numpy")) else t[0]
+    return {"value": round(T / s, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one config-2 layer forward of {T} tokens by the numpy oracle port of the "
+                      f"reference's torch CPU path (fp32 BLAS, {os.cpu_count()} host threads); "
+                      f"{s:.2f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    T = args.tokens
+    sample = min(T, 2)
+    for _ in range(args.warmup):
+        cpu_forward_time(sample, reps=1, seed=1)
+    times = []
+    for i in range(args.steps):
+        times.extend(cpu_forward_time(sample, reps=1, seed=2 + (i % 4)))
+    s = sum(times) / len(times)
+    value = sample / s
+    out = {
+        "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(s * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing",
+                   "tokens_per_gpu": T, "sample_tokens_per_step": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"{sample} of the {T} tokens per step through the numpy oracle port of "
+                                   f"the reference's torch CPU MoE.forward (fp32 BLAS, all host threads)"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,189 @@
+/*
+ * wfb200.h - C ABI of the B200-native WANferenz MoE decode path.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no torch types.
+ * The workspace of wf_moe_forward must be zero-filled once when allocated;
+ * the kernels leave their counters at zero after every call.
+ * Every entry point returns an int status (WF_OK or a negative WF_E_* code);
+ * wf_last_error() returns the message of the last failure on the calling
+ * host thread.  No entry point allocates device memory, synchronizes the
+ * stream or reads device data back, except the load-time checks
+ * wf_fp4_scales_in_range() and wf_moe_read_error(), which say so.
+ *
+ * Data formats (identical to the reference's tensors, so a reference
+ * checkpoint's bytes are passed through unchanged):
+ *   bf16        2-byte bfloat16, row-major
+ *   e4m3        1-byte float8_e4m3fn
+ *   e8m0        1-byte float8_e8m0fnu (power-of-two scale 2^(b-127))
+ *   fp4 packed  float4_e2m1fn_x2: two E2M1 codes per byte, low nibble = even k
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the WANferenz project root).
+ */
+#ifndef WFB200_H
+#define WFB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define WF_OK 0
+#define WF_E_SHAPE (-1)     /* unsupported or inconsistent dimensions          */
+#define WF_E_DTYPE (-2)     /* unsupported scale kind / format flag            */
+#define WF_E_EXPERT_ID (-3) /* an expert id or token id outside its range      */
+#define WF_E_TIMEOUT (-4)   /* a device-side wait ran past its bound           */
+#define WF_E_CUDA (-5)      /* a CUDA runtime call failed                      */
+#define WF_E_RANGE (-6)     /* FP4 weight scales outside the exact range       */
+#define WF_E_ARG (-7)       /* null pointer or workspace too small             */
+
+/* scale kinds of activation / weight scale tensors */
+#define WF_SCALE_F32 0  /* float32 scales                                   */
+#define WF_SCALE_E8M0 1 /* e8m0 byte scales                                 */
+
+/* router score functions: ModelArgs.score_func (architecture.py:59) */
+#define WF_SCORE_SOFTMAX 0
+#define WF_SCORE_SIGMOID 1
+#define WF_SCORE_SQRTSOFTPLUS 2
+
+/* One MoE layer's shapes and options: the ModelArgs fields read by Gate,
+ * Expert and MoE (wanferenz/model/architecture.py:42-93, 674-794). */
+typedef struct wf_moe_config {
+    int32_t dim;             /* D: hidden size                         */
+    int32_t inter_dim;       /* I: moe_inter_dim                       */
+    int32_t n_experts;       /* E: n_routed_experts                    */
+    int32_t n_local_experts; /* experts held by this rank (E / world)   */
+    int32_t expert_offset;   /* first local expert id (rank * E_local)  */
+    int32_t topk;            /* n_activated_experts                    */
+    int32_t score_func;      /* WF_SCORE_*                             */
+    int32_t hash_layer;      /* 1: indices = tid2eid[input_ids]        */
+    int32_t ue8m0;           /* 1: power-of-two activation scales      */
+    int32_t max_tokens;      /* capacity the workspace is sized for    */
+    int64_t vocab;           /* rows of tid2eid (hash layers)          */
+    float route_scale;       /* Gate.route_scale                       */
+    float swiglu_limit;      /* Expert.swiglu_limit (0 = off)          */
+} wf_moe_config;
+
+/* Device pointers to one layer's weights, in the reference's bank layout
+ * (wanferenz/kernels/fp4_grouped.py:136-201 for the routed bank,
+ *  wanferenz/kernels/fp8_vector.py:316-351 for the shared w13 stack). */
+typedef struct wf_moe_weights {
+    const void *gate_w;       /* [E, D] bf16                               */
+    const float *gate_bias;   /* [E] f32, or NULL on hash layers            */
+    const int32_t *tid2eid;   /* [vocab, topk] int32 on hash layers, else NULL */
+    const uint8_t *w13;       /* [E_local, 2I, D/2] fp4 packed (w1 rows, then w3 rows) */
+    const uint8_t *w13_s;     /* [E_local, 2I, D/32] e8m0                   */
+    const uint8_t *w2;        /* [E_local, D, I/2] fp4 packed               */
+    const uint8_t *w2_s;      /* [E_local, D, I/32] e8m0                    */
+    const uint8_t *shared_w13; /* [2I, D] e4m3 (w1 rows, then w3 rows)       */
+    const void *shared_s13;   /* [2I/128, D/128] scale (shared_scale_kind)   */
+    const uint8_t *shared_w2; /* [D, I] e4m3                               */
+    const void *shared_s2;    /* [D/128, I/128] scale                       */
+    int32_t shared_scale_kind; /* WF_SCALE_E8M0 or WF_SCALE_F32             */
+} wf_moe_weights;
+
+/* Last failure message of this host thread ("" when none). */
+const char *wf_last_error(void);
+
+/* Number of SMs of the current device (the persistent grid size). */
+int wf_device_sm_count(void);
+
+/* Bytes of device workspace wf_moe_forward needs for cfg->max_tokens tokens.
+ * Allocate once (e.g. at layer load) and reuse; calls sharing one workspace
+ * must be ordered on one stream. */
+size_t wf_moe_workspace_bytes(const wf_moe_config *cfg);
+
+/* Full MoE layer forward for T tokens: router, routed FP4 SwiGLU experts,
+ * FP8 shared expert and the ascending-expert fp32 combine.
+ * Replaces MoE.forward (wanferenz/model/architecture.py:777-794) and its GPU
+ * patch grouped_forward (wanferenz/kernels/fp4_grouped.py:271-324).
+ *   x          [T, D] bf16 (device)
+ *   input_ids  [T] int64 (device; read on hash layers only, may be NULL otherwise)
+ *   y          [T, D] bf16 output, or NULL when y_partial is given
+ *   y_partial  [T, D] f32 output of the local experts' routed sum only
+ *              (expert-parallel mode: the caller all-reduces it and calls
+ *              wf_moe_finish), or NULL
+ *   out_weights [T, topk] f32 and out_indices [T, topk] int64: the router's
+ *              outputs (Gate.forward, architecture.py:696-718); may be NULL
+ * Launches 3 kernels on `stream`; allocates nothing; no host sync. */
+int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                   const int64_t *input_ids, int32_t T, void *y, float *y_partial,
+                   float *out_weights, int64_t *out_indices, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* wf_moe_forward with four caller-created cudaEvent_t recorded on `stream`
+ * before the first and after each of the three kernels (measurement hook:
+ * per-kernel durations without a profiler).  The records are "external", so
+ * they also become event nodes when the stream is being captured into a CUDA
+ * graph.  No counterpart in the reference. */
+int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                         const int64_t *input_ids, int32_t T, void *y, float *y_partial,
+                         float *out_weights, int64_t *out_indices, void *workspace,
+                         size_t workspace_bytes, void *stream, void *const *events);
+
+/* Expert-parallel epilogue: y[t] = bf16(y_partial_reduced[t] + shared_out[row0 + t])
+ * for t < T, where shared_out is the shared expert's output that the last
+ * wf_moe_forward on this workspace left in it (architecture.py:791-794, after
+ * dist.all_reduce; row0 selects this rank's rows of an all-gathered batch). */
+int wf_moe_finish(const wf_moe_config *cfg, const float *y_partial_reduced, int32_t T,
+                  int32_t row0, void *y, const void *workspace, size_t workspace_bytes,
+                  void *stream);
+
+/* Router only: Gate.forward (architecture.py:696-718).  Writes weights
+ * [T, topk] f32 and indices [T, topk] int64 (descending biased score). */
+int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                 const int64_t *input_ids, int32_t T, float *out_weights,
+                 int64_t *out_indices, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Copies the workspace's device error word to the host (synchronizes the
+ * stream).  Returns 0 or a negative WF_E_* code for the last forward. */
+int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream);
+
+/* act_quant (wanferenz/kernels/torch_ops.py:33-49; TileLang reference.py:117-146):
+ * x [M, K] bf16 -> q [M, K] e4m3 and s [M, K/block] scales of `scale_kind`.
+ * ue8m0 != 0 rounds each scale up to a power of two (scale_fmt="ue8m0"). */
+int wf_act_quant(const void *x, int64_t M, int64_t K, int32_t block, int32_t ue8m0, void *q,
+                 void *s, int32_t scale_kind, void *stream);
+
+/* fp4_act_quant (torch_ops.py:61-74; TileLang reference.py:212-232):
+ * x [M, K] bf16 -> packed E2M1 [M, K/2] and e8m0 scales [M, K/32]. */
+int wf_fp4_act_quant(const void *x, int64_t M, int64_t K, void *q, void *s, void *stream);
+
+/* fp8_gemm (torch_ops.py:93-99; TileLang reference.py:292-311):
+ * out[M, N] bf16 = (a * a_s) @ (b * b_s)^T with a [M, K] e4m3,
+ * a_s [M, K/128], b [N, K] e4m3, b_s [ceil(N/128), K/128]. */
+int wf_fp8_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *b,
+                const void *b_s, int32_t b_scale_kind, int64_t M, int64_t N, int64_t K,
+                void *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* fp4_gemm (torch_ops.py:102-108; TileLang reference.py:572-591):
+ * out[M, N] bf16 = (a * a_s) @ (unpack(b) * b_s)^T with b [N, K/2] fp4
+ * packed and b_s [N, K/32] e8m0. */
+int wf_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *b,
+                const void *b_s, int64_t M, int64_t N, int64_t K, void *out, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* grouped_fp4_gemm (wanferenz/kernels/fp4_grouped.py:96-128): slot g
+ * multiplies a[g] [K] e4m3 by its own weights w[g] [N, K/2] fp4:
+ * out[g, N] bf16 = (a[g] * a_s[g]) @ (unpack(w[g]) * w_s[g])^T. */
+int wf_grouped_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *w,
+                        const void *w_s, int64_t G, int64_t N, int64_t K, void *out,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* Workspace bytes for the dense GEMM entry points above. */
+size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* Load-time check that every FP4 weight scale byte lies in [104, 140]
+ * (2^-23 .. 2^13), the range in which the kernels' f16 prescale of E2M1
+ * values is exact.  Synchronizes the stream.  Returns 1 (in range), 0 (not)
+ * or a negative WF_E_* code. */
+int wf_fp4_scales_in_range(const uint8_t *scales, int64_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WFB200_H */

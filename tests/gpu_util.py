@@ -1,0 +1,82 @@
+"""Helpers for the GPU parity tests: upload seeded synthetic layers, compare outputs."""
+
+import numpy as np
+import torch
+
+from oracle import fixtures as F
+from oracle import moe_oracle as O
+
+
+def bf16_tensor(u16, device="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def u8_tensor(a, device="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a, np.uint8)).to(device)
+
+
+def device_layer(layer: F.SyntheticLayer, touched, max_tokens=64, expert_range=None, seed=0):
+    """MoELayer whose experts in ``touched`` hold the fixture weights; the others random bytes."""
+    from wanferenz_b200.moe import MoELayer, MoEWeights
+
+    s = layer.spec
+    D, I, E = s.D, s.I, s.E
+    lo, hi = expert_range or (0, E)
+    El = hi - lo
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w13 = torch.randint(0, 256, (El, 2 * I, D // 2), dtype=torch.uint8, device="cuda", generator=g)
+    w13_s = torch.randint(118, 125, (El, 2 * I, D // 32), dtype=torch.uint8, device="cuda", generator=g)
+    w2 = torch.randint(0, 256, (El, D, I // 2), dtype=torch.uint8, device="cuda", generator=g)
+    w2_s = torch.randint(118, 125, (El, D, I // 32), dtype=torch.uint8, device="cuda", generator=g)
+    for e in sorted(set(int(e) for e in touched)):
+        if not lo <= e < hi:
+            continue
+        w1, s1, w3, s3, ww2, s2 = layer.expert(e)
+        w13[e - lo] = u8_tensor(np.concatenate([w1, w3]))
+        w13_s[e - lo] = u8_tensor(np.concatenate([s1, s3]))
+        w2[e - lo] = u8_tensor(ww2)
+        w2_s[e - lo] = u8_tensor(s2)
+    sw1, ss1, sw3, ss3, sw2, ss2 = layer.shared()
+    weights = MoEWeights(
+        gate_w=bf16_tensor(layer.gate_w_bf16),
+        gate_b=None if layer.gate_b is None else torch.from_numpy(layer.gate_b).cuda(),
+        tid2eid=None if layer.tid2eid is None else torch.from_numpy(layer.tid2eid).cuda(),
+        w13=w13, w13_s=w13_s, w2=w2, w2_s=w2_s,
+        shared_w13=u8_tensor(np.concatenate([sw1, sw3])), shared_s13=u8_tensor(np.concatenate([ss1, ss3])),
+        shared_w2=u8_tensor(sw2), shared_s2=u8_tensor(ss2))
+    return MoELayer(weights, dim=D, inter_dim=I, n_experts=E, topk=s.topk, score_func=s.score_func,
+                    route_scale=s.route_scale, swiglu_limit=s.swiglu_limit, hash_layer=s.hash_layer,
+                    vocab=s.vocab, ue8m0=s.ue8m0, n_local_experts=El, expert_offset=lo,
+                    max_tokens=max_tokens)
+
+
+def to_f32(t):
+    return t.float().cpu().numpy()
+
+
+def assert_layer_close(y, y_ref, what=""):
+    """The north-star tolerance for bf16 layer outputs.
+
+    * mean absolute error <= 2e-3;
+    * max relative error <= 1e-2, where the relative error of an element is
+      |y - y_ref| / max(|y_ref|, 0.01 * rms(y_ref)) (the floor keeps
+      cancellation-sized outputs from dividing by ~0).
+    """
+    y = np.asarray(y, np.float32)
+    y_ref = np.asarray(y_ref, np.float32)
+    d = np.abs(y - y_ref)
+    mae = float(d.mean())
+    rms = float(np.sqrt(np.mean(y_ref.astype(np.float64) ** 2)))
+    rel = d / np.maximum(np.abs(y_ref), 0.01 * rms)
+    assert np.isfinite(y).all(), f"{what}: non-finite output"
+    assert mae <= 2e-3, f"{what}: MAE {mae:.3e} > 2e-3"
+    assert rel.max() <= 1e-2, f"{what}: max rel err {rel.max():.3e} > 1e-2"
+    return mae, float(rel.max()), float((y != y_ref).mean())
+
+
+def near_tie_rows(x, layer, ids=None, eps=1e-6):
+    s = layer.spec
+    if s.hash_layer:
+        return np.zeros(x.shape[0], bool)
+    _, _, biased = O.gate(x, layer.gate_w, layer.gate_b, s.topk, s.score_func, s.route_scale)
+    return O.topk_margin(biased, s.topk) < eps

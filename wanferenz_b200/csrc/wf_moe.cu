@@ -1,0 +1,1502 @@
+// wf_moe.cu - B200 (sm_100a) kernels of the WANferenz MoE decode layer and
+// the C ABI declared in include/wfb200.h.
+//
+// The layer (wanferenz/model/architecture.py:674-794) runs as three
+// persistent launches of one CTA per SM:
+//
+//   K1 "up"   router logits (fp64 accumulation) + top-k/dispatch tables by the
+//             last router CTA; shared-expert w1/w3 + SwiGLU  -> hs (bf16)
+//   K2 "mid"  routed-expert w1/w3 + SwiGLU * route weight     -> h  (bf16)
+//             shared-expert w2                                  -> os (bf16)
+//   K3 "down" routed-expert w2                                  -> o  (bf16)
+//             + per-row-block ascending-expert combine          -> y
+//
+// Each launch is a static, balanced split of "items" over the CTAs.  An item
+// is up to 32 weight rows (<= 34 KB) times up to 8 tokens.  Inside a CTA one
+// producer warp streams each item's rows into a 6-slot shared-memory ring with
+// bulk TMA copies (cp.async.bulk, completion on an mbarrier); eight consumer
+// warps split K, dequantize in registers (E2M1 -> f16 with the per-32 UE8M0
+// scale folded in, exact; E4M3 -> f16, exact), multiply on the tensor cores
+// (mma.m16n8k16, f32 accumulate), apply the per-128 activation scale in f32,
+// and reduce across warps in a fixed order through shared memory.
+// Activations are quantized to E4M3 (act_quant, torch_ops.py:33-49) by the
+// consumer warps themselves when they load a token's K-slice.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/wfb200.h"
+#include "wf_ptx.cuh"
+
+namespace wf {
+
+constexpr int NCW = 8;                 // consumer warps
+constexpr int NTHR = (NCW + 1) * 32;   // + 1 producer warp
+constexpr int NCT = NCW * 32;          // consumer threads
+constexpr int NSLOT = 6;               // ring slots
+constexpr int SLOT_W = 34816;          // weight bytes per slot (padded rows)
+constexpr int SLOT_S = 2048;           // FP4 scale bytes per slot
+constexpr int SLOT_BYTES = SLOT_W + SLOT_S;
+constexpr int MAXR = 32;               // weight rows per item
+constexpr int NTM = 1;                 // n-tiles (8 tokens each) per item
+constexpr int TPI = 8 * NTM;           // tokens per item
+constexpr int SPW = 4;                 // max 128-wide K segments per warp
+constexpr int KMAX = NCW * SPW * 128;  // longest K one item covers (4096)
+constexpr int RED_BYTES = NCW * MAXR * TPI * 4;
+constexpr int OFF_RED = NSLOT * SLOT_BYTES;
+constexpr int OFF_BAR = OFF_RED + RED_BYTES;
+constexpr int OFF_MISC = OFF_BAR + 2 * NSLOT * 8 + 64;
+constexpr int MISC_BYTES = 2048;  // router partial sums (fp64) / top-k expert counts
+constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES;
+constexpr int MAX_E = 512;
+constexpr int MAX_K = 8;
+constexpr int MAX_T = 256;
+
+enum { EP_RSWIGLU = 1, EP_SSWIGLU = 2, EP_SOUT = 3, EP_ROUT = 4, EP_DENSE = 5 };
+enum { BS_XPAIR = 1, BS_XTOK = 2, BS_H = 3, BS_HS = 4, BS_PREQ = 5 };
+enum { FMT_FP4 = 0, FMT_FP8 = 1 };
+enum { KID_UP = 1, KID_MID = 2, KID_DOWN = 3, KID_DENSE = 4 };
+
+// hdr fields written by the top-k CTA
+enum { H_NACT = 0, H_IT2 = 1, H_IT3 = 2, H_TGT = 3, H_NPAIR = 4, H_SIZE = 8 };
+
+struct Geo {
+    int st_w13, st_w2, st_s13, st_s2;  // smem row strides (bytes)
+    int nh13, r2, nhs13, rs2;          // rows per item
+};
+
+struct MoeArgs {
+    int T, D, I, E, El, e0, topk, score_func, hash, ue8m0, partial, shared_f32, route_only;
+    float route_scale, swiglu_limit;
+    long long vocab;
+    const __nv_bfloat16 *x;
+    const long long *ids;
+    const __nv_bfloat16 *gate_w;
+    const float *gate_b;
+    const int *tid2eid;
+    const uint8_t *w13, *w13_s, *w2, *w2_s, *sw13, *sw2;
+    const void *ss13, *ss2;
+    __nv_bfloat16 *y;
+    float *y_partial;
+    float *out_w;
+    long long *out_idx;
+    // workspace
+    float *logits;
+    int *hdr, *act_expert, *act_off, *act_it2, *act_it3;
+    int *pair_tok, *tok_np, *tok_pairs, *ridx;
+    float *pair_w, *rw;
+    __nv_bfloat16 *h, *hs, *o, *os;
+    unsigned *cnt_router, *cnt_rb;
+    int *err;
+    Geo g;
+};
+
+// Dense GEMM (operator entry points) arguments.
+struct DenseArgs {
+    int M, N, K, G;               // G > 0: grouped (slot g uses weights g, token g)
+    int wfmt, a_f32, b_f32;       // weight format; scale kinds
+    const uint8_t *a;             // e4m3 [M, K]
+    const void *a_s;              // [M, K/128]
+    const uint8_t *b;             // weights
+    const void *b_s;              // scales
+    __nv_bfloat16 *out;           // [M, N]
+    int rows, stride;             // rows per item, smem row stride
+    int *err;
+};
+
+struct Item {
+    int ep, bsrc, fmt, K, stride;
+    int nrun, rrows;
+    const uint8_t *wsrc[2];
+    const uint8_t *ssrc[2];
+    int grow[2];
+    int row0, a, tok0, ntok, rb;
+};
+
+__device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------------------
+// item decoding (identical in producer and consumers)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int find_active(const int *prefix, int n_act, int i) {
+    int lo = 0, hi = n_act - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (__ldg(prefix + mid) <= i) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it2) {
+    Item it;
+    const int D = a.D, I = a.I;
+    it.ssrc[0] = it.ssrc[1] = nullptr;
+    it.grow[0] = it.grow[1] = 0;
+    it.rb = 0;
+    if (kid == KID_UP) {  // shared expert w1/w3 rows + SwiGLU
+        const int TG = cdiv(a.T, TPI);
+        const int hb = i / TG, tg = i % TG, nh = a.g.nhs13;
+        it.ep = EP_SSWIGLU; it.bsrc = BS_XTOK; it.fmt = FMT_FP8; it.K = D; it.stride = a.g.st_s13;
+        it.nrun = 2; it.rrows = nh;
+        it.grow[0] = hb * nh; it.grow[1] = I + hb * nh;
+        it.wsrc[0] = a.sw13 + (size_t)it.grow[0] * D;
+        it.wsrc[1] = a.sw13 + (size_t)it.grow[1] * D;
+        it.row0 = hb * nh; it.a = 0; it.tok0 = tg * TPI; it.ntok = min(TPI, a.T - tg * TPI);
+        return it;
+    }
+    if (kid == KID_MID && i >= n_it2) {  // shared expert w2
+        const int j = i - n_it2, TG = cdiv(a.T, TPI);
+        const int rb = j / TG, tg = j % TG, nr = a.g.rs2;
+        it.ep = EP_SOUT; it.bsrc = BS_HS; it.fmt = FMT_FP8; it.K = I; it.stride = a.g.st_s2;
+        it.nrun = 1; it.rrows = nr;
+        it.grow[0] = rb * nr;
+        it.wsrc[0] = a.sw2 + (size_t)it.grow[0] * I;
+        it.wsrc[1] = it.wsrc[0];
+        it.row0 = rb * nr; it.a = 0; it.tok0 = tg * TPI; it.ntok = min(TPI, a.T - tg * TPI);
+        return it;
+    }
+    // routed items
+    const int *pref = (kid == KID_MID) ? a.act_it2 : a.act_it3;
+    const int ai = find_active(pref, n_act, i);
+    const int local = i - __ldg(pref + ai);
+    const int p0 = __ldg(a.act_off + ai), ta = __ldg(a.act_off + ai + 1) - p0;
+    const int TGa = cdiv(ta, TPI);
+    const int blk = local / TGa, tg = local % TGa;
+    const int el = __ldg(a.act_expert + ai) - a.e0;
+    it.a = ai; it.tok0 = p0 + tg * TPI; it.ntok = min(TPI, ta - tg * TPI);
+    if (kid == KID_MID) {  // routed w1/w3 rows + SwiGLU
+        const int nh = a.g.nh13;
+        const uint8_t *wb = a.w13 + (size_t)el * (2 * I) * (D / 2);
+        const uint8_t *sb = a.w13_s + (size_t)el * (2 * I) * (D / 32);
+        it.ep = EP_RSWIGLU; it.bsrc = BS_XPAIR; it.fmt = FMT_FP4; it.K = D; it.stride = a.g.st_w13;
+        it.nrun = 2; it.rrows = nh;
+        it.grow[0] = blk * nh; it.grow[1] = I + blk * nh;
+        it.wsrc[0] = wb + (size_t)it.grow[0] * (D / 2);
+        it.wsrc[1] = wb + (size_t)it.grow[1] * (D / 2);
+        it.ssrc[0] = sb + (size_t)it.grow[0] * (D / 32);
+        it.ssrc[1] = sb + (size_t)it.grow[1] * (D / 32);
+        it.row0 = blk * nh;
+    } else {  // routed w2 rows
+        const int nr = a.g.r2;
+        const uint8_t *wb = a.w2 + (size_t)el * D * (I / 2);
+        const uint8_t *sb = a.w2_s + (size_t)el * D * (I / 32);
+        it.ep = EP_ROUT; it.bsrc = BS_H; it.fmt = FMT_FP4; it.K = I; it.stride = a.g.st_w2;
+        it.nrun = 1; it.rrows = nr;
+        it.grow[0] = blk * nr;
+        it.wsrc[0] = wb + (size_t)it.grow[0] * (I / 2);
+        it.wsrc[1] = it.wsrc[0];
+        it.ssrc[0] = sb + (size_t)it.grow[0] * (I / 32);
+        it.ssrc[1] = it.ssrc[0];
+        it.row0 = blk * nr; it.rb = blk;
+    }
+    return it;
+}
+
+__device__ Item decode_dense(const DenseArgs &d, int i) {
+    Item it;
+    const int nrb = d.N / d.rows;
+    int rb, tok0, ntok, gsel = 0;
+    if (d.G > 0) {  // grouped: item = (g, rb), one token (row g of a)
+        gsel = i / nrb; rb = i % nrb; tok0 = gsel; ntok = 1;
+    } else {
+        const int TG = cdiv(d.M, TPI);
+        rb = i / TG; const int tg = i % TG;
+        tok0 = tg * TPI; ntok = min(TPI, d.M - tok0);
+    }
+    it.ep = EP_DENSE; it.bsrc = BS_PREQ; it.fmt = d.wfmt; it.K = d.K; it.stride = d.stride;
+    it.nrun = 1; it.rrows = d.rows; it.rb = rb;
+    it.grow[0] = rb * d.rows; it.grow[1] = 0;
+    const size_t rowb = d.wfmt == FMT_FP4 ? (size_t)d.K / 2 : (size_t)d.K;
+    const uint8_t *wbase = d.b + (size_t)gsel * d.N * rowb;
+    it.wsrc[0] = wbase + (size_t)it.grow[0] * rowb;
+    it.wsrc[1] = it.wsrc[0];
+    if (d.wfmt == FMT_FP4) {
+        const uint8_t *sbase = (const uint8_t *)d.b_s + (size_t)gsel * d.N * (d.K / 32);
+        it.ssrc[0] = sbase + (size_t)it.grow[0] * (d.K / 32);
+    } else {
+        it.ssrc[0] = nullptr;
+    }
+    it.ssrc[1] = it.ssrc[0];
+    it.row0 = it.grow[0]; it.a = gsel; it.tok0 = tok0; it.ntok = ntok;
+    return it;
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory context
+// ---------------------------------------------------------------------------
+struct Smem {
+    uint8_t *base;
+    __device__ uint8_t *slot(int s) const { return base + s * SLOT_BYTES; }
+    __device__ float *red() const { return reinterpret_cast<float *>(base + OFF_RED); }
+    __device__ uint64_t *full(int s) const { return reinterpret_cast<uint64_t *>(base + OFF_BAR) + s; }
+    __device__ uint64_t *empty(int s) const {
+        return reinterpret_cast<uint64_t *>(base + OFF_BAR) + NSLOT + s;
+    }
+    __device__ volatile int *flags() const {
+        return reinterpret_cast<volatile int *>(base + OFF_BAR + 2 * NSLOT * 8);
+    }
+    __device__ double *misc() const { return reinterpret_cast<double *>(base + OFF_MISC); }
+};
+
+__device__ __forceinline__ void item_range(int n, int &i0, int &i1) {
+    i0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
+    i1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
+}
+
+// ---------------------------------------------------------------------------
+// producer: stream each item's weight rows (and FP4 scales) into the ring
+// ---------------------------------------------------------------------------
+template <typename Decode>
+__device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode) {
+    if ((threadIdx.x & 31) != 0) return;
+    volatile int *abort = sm.flags();
+    int q = 0;
+    for (int i = i0; i < i1; ++i, ++q) {
+        const Item it = decode(i);
+        const int s = q % NSLOT;
+        if (q >= NSLOT && !*abort) {
+            if (!wf_wait(sm.empty(s), ((q / NSLOT) - 1) & 1, err)) *abort = 1;
+        }
+        if (*abort) continue;
+        const uint32_t rowb = it.fmt == FMT_FP4 ? it.K / 2 : it.K;
+        const uint32_t ks = it.K / 32;
+        const int na = it.nrun * it.rrows;
+        uint32_t bytes = na * rowb + (it.fmt == FMT_FP4 ? na * ks : 0);
+        mbar_arrive_expect_tx(sm.full(s), bytes);
+        uint8_t *dst = sm.slot(s);
+        for (int run = 0; run < it.nrun; ++run) {
+            for (int r = 0; r < it.rrows; ++r)
+                bulk_g2s(dst + (run * it.rrows + r) * it.stride, it.wsrc[run] + (size_t)r * rowb,
+                         rowb, sm.full(s));
+            if (it.fmt == FMT_FP4)
+                bulk_g2s(dst + SLOT_W + run * it.rrows * ks, it.ssrc[run], it.rrows * ks,
+                         sm.full(s));
+        }
+    }
+    // drain: every armed phase must complete before the CTA may exit
+    const int nq = q;
+    for (int s = 0; s < NSLOT && s < nq; ++s) {
+        const int last = s + ((nq - 1 - s) / NSLOT) * NSLOT;
+        wf_wait(sm.full(s), (last / NSLOT) & 1, err);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// consumers
+// ---------------------------------------------------------------------------
+struct BRegs {
+    uint32_t b[NTM][SPW][16];  // token slot g's K-slice as f16x2 E4M3 codes
+    float sx[NTM][SPW][2];     // activation scales of the C-fragment tokens
+};
+
+__device__ __forceinline__ float round_scale_e8(float amax, int ue8m0) {
+    const float x = amax * (1.0f / 448.0f);
+    if (!ue8m0) return x;
+    const uint32_t b = __float_as_uint(x);
+    if ((b & 0x7fffffu) == 0) return x;
+    return __uint_as_float(((b >> 23) + 1) << 23);
+}
+
+// Quantize 32 bf16 values (act_quant semantics) into 16 f16x2 E4M3 codes;
+// the 4 lanes of a quad share one 128-block.  Returns the block scale.
+__device__ __forceinline__ float quant32(const __nv_bfloat16 *src, bool valid, int ue8m0,
+                                         uint32_t (&out)[16]) {
+    uint32_t w[16];
+    if (valid) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 u = ldg128(src + c * 8);
+            w[4 * c] = u.x; w[4 * c + 1] = u.y; w[4 * c + 2] = u.z; w[4 * c + 3] = u.w;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e] = 0u;
+    }
+    // |bf16| max on the bit patterns: clearing the sign bits leaves an order-preserving integer
+    uint32_t amax_bits = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        amax_bits = max(amax_bits, w[e] & 0x7fffu);
+        amax_bits = max(amax_bits, (w[e] >> 16) & 0x7fffu);
+    }
+    float amax = bf16_bits_to_f32(amax_bits);
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float s = round_scale_e8(fmaxf(amax, 1e-4f), ue8m0);
+    const float inv = 1.0f / s;  // exact when s is a power of two
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        float lo = bf16_bits_to_f32(w[e] & 0xffffu), hi = bf16_bits_to_f32(w[e] >> 16);
+        if (ue8m0) { lo *= inv; hi *= inv; }
+        else { lo = __fdiv_rn(lo, s); hi = __fdiv_rn(hi, s); }
+        lo = fminf(fmaxf(lo, -448.f), 448.f);
+        hi = fminf(fmaxf(hi, -448.f), 448.f);
+        out[e] = e4m3x2_to_f16x2(f32x2_to_e4m3x2(lo, hi));
+    }
+    return valid ? s : 0.f;
+}
+
+// Pre-quantized E4M3 codes (32 bytes) -> 16 f16x2
+__device__ __forceinline__ void codes32(const uint8_t *src, bool valid, uint32_t (&out)[16]) {
+    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
+    if (valid) { u0 = ldg128(src); u1 = ldg128(src + 16); }
+    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        out[2 * e] = e4m3x2_to_f16x2((uint16_t)(w[e] & 0xffffu));
+        out[2 * e + 1] = e4m3x2_to_f16x2((uint16_t)(w[e] >> 16));
+    }
+}
+
+template <typename RowPtr, typename PreqScale>
+__device__ void load_b(const Item &it, int warp, int lane, int ue8m0, BRegs &B, RowPtr rowptr,
+                       PreqScale preq_scale) {
+    const int g = lane >> 2, tig = lane & 3;
+    const int nseg = it.K / 128, spw = cdiv(nseg, NCW), s0 = warp * spw;
+    const int nnt = cdiv(it.ntok, 8);
+#pragma unroll
+    for (int nt = 0; nt < NTM; ++nt) {
+        const int j = nt * 8 + g;
+        const bool tv = (nt < nnt) && (j < it.ntok);
+#pragma unroll
+        for (int sj = 0; sj < SPW; ++sj) {
+            const int s = s0 + sj;
+            const bool sv = (sj < spw) && (s < nseg) && (nt < nnt);
+            float sc = 0.f;
+            if (sv) {
+                const int k0 = s * 128 + tig * 32;
+                if (it.bsrc == BS_PREQ) {
+                    const uint8_t *src = tv ? (const uint8_t *)rowptr(it, j) : nullptr;
+                    codes32(src ? src + k0 : nullptr, tv, B.b[nt][sj]);
+                    sc = tv ? preq_scale(it, j, s) : 0.f;
+                } else {
+                    const __nv_bfloat16 *src = tv ? (const __nv_bfloat16 *)rowptr(it, j) : nullptr;
+                    sc = quant32(tv ? src + k0 : nullptr, tv, ue8m0, B.b[nt][sj]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) B.b[nt][sj][e] = 0u;
+            }
+            B.sx[nt][sj][0] = __shfl_sync(0xffffffffu, sc, (2 * tig) * 4);
+            B.sx[nt][sj][1] = __shfl_sync(0xffffffffu, sc, (2 * tig + 1) * 4);
+        }
+    }
+}
+
+// f16x2 {s, s} for an e8m0 scale byte (exact for bytes in [104, 140])
+__device__ __forceinline__ uint32_t scale_f16x2(uint32_t b) {
+    const __half h = __float2half_rn(e8m0_to_f32(b));
+    const uint32_t u = __half_as_ushort(h);
+    return u | (u << 16);
+}
+
+// FP8 block scale of global weight row `grow`, K-block `kb`
+template <typename FP8Scale>
+__device__ __forceinline__ float fp8_row_scale(const Item &it, int arow, int kb, FP8Scale f8s) {
+    const int run = arow / it.rrows;
+    const int grow = it.grow[run] + (arow - run * it.rrows);
+    return f8s(grow / 128, kb);
+}
+
+// One item's main loop for one consumer warp: acc[m][nt][c] over the warp's K segments.
+template <typename FP8Scale>
+__device__ __forceinline__ void compute_item(const Item &it, const uint8_t *slot, int warp,
+                                             int lane, const BRegs &B, float (&acc)[2][NTM][4],
+                                             FP8Scale f8s) {
+    const int g = lane >> 2, tig = lane & 3;
+    const int nseg = it.K / 128, spw = cdiv(nseg, NCW), s0 = warp * spw;
+    const int na = it.nrun * it.rrows, nmt = cdiv(na, 16), nnt = cdiv(it.ntok, 8);
+    const uint8_t *sc = slot + SLOT_W;
+    const int ks = it.K / 32;
+#pragma unroll
+    for (int sj = 0; sj < SPW; ++sj) {
+        const int s = s0 + sj;
+        if (!(sj < spw && s < nseg)) continue;
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            if (m >= nmt) continue;
+            const int ra = 16 * m + g, rb = ra + 8;
+            const bool va = ra < na, vb = rb < na;
+            float cs[NTM][4];
+#pragma unroll
+            for (int nt = 0; nt < NTM; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) cs[nt][c] = 0.f;
+            if (it.fmt == FMT_FP4) {
+                uint4 wa = make_uint4(0, 0, 0, 0), wb = wa;
+                uint32_t sa = 127, sbb = 127;
+                if (va) { wa = lds128(slot + ra * it.stride + s * 64 + tig * 16); sa = sc[ra * ks + s * 4 + tig]; }
+                if (vb) { wb = lds128(slot + rb * it.stride + s * 64 + tig * 16); sbb = sc[rb * ks + s * 4 + tig]; }
+                const uint32_t pa = scale_f16x2(sa), pb = scale_f16x2(sbb);
+                const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+                const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t fa[4], fb[4];
+                    fp4x8_to_f16x8(wav[q], fa);
+                    fp4x8_to_f16x8(wbv[q], fb);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) { fa[e] = hmul2_u32(fa[e], pa); fb[e] = hmul2_u32(fb[e], pb); }
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int j = 2 * q + jj;
+#pragma unroll
+                        for (int nt = 0; nt < NTM; ++nt)
+                            if (nt < nnt)
+                                mma_f16(cs[nt], fa[2 * jj], fb[2 * jj], fa[2 * jj + 1], fb[2 * jj + 1],
+                                        B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < NTM; ++nt) {
+                    acc[m][nt][0] = fmaf(cs[nt][0], B.sx[nt][sj][0], acc[m][nt][0]);
+                    acc[m][nt][1] = fmaf(cs[nt][1], B.sx[nt][sj][1], acc[m][nt][1]);
+                    acc[m][nt][2] = fmaf(cs[nt][2], B.sx[nt][sj][0], acc[m][nt][2]);
+                    acc[m][nt][3] = fmaf(cs[nt][3], B.sx[nt][sj][1], acc[m][nt][3]);
+                }
+            } else {
+                uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
+                float fsa = 0.f, fsb = 0.f;
+                if (va) {
+                    const uint8_t *p = slot + ra * it.stride + s * 128 + tig * 32;
+                    a0 = lds128(p); a1 = lds128(p + 16);
+                    fsa = fp8_row_scale(it, ra, s, f8s);
+                }
+                if (vb) {
+                    const uint8_t *p = slot + rb * it.stride + s * 128 + tig * 32;
+                    b0 = lds128(p); b1 = lds128(p + 16);
+                    fsb = fp8_row_scale(it, rb, s, f8s);
+                }
+                const uint32_t wav[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const uint32_t wbv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t x0 = e4m3x2_to_f16x2((uint16_t)(wav[j] & 0xffffu));
+                    const uint32_t x2 = e4m3x2_to_f16x2((uint16_t)(wav[j] >> 16));
+                    const uint32_t x1 = e4m3x2_to_f16x2((uint16_t)(wbv[j] & 0xffffu));
+                    const uint32_t x3 = e4m3x2_to_f16x2((uint16_t)(wbv[j] >> 16));
+#pragma unroll
+                    for (int nt = 0; nt < NTM; ++nt)
+                        if (nt < nnt)
+                            mma_f16(cs[nt], x0, x1, x2, x3, B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NTM; ++nt) {
+                    acc[m][nt][0] = fmaf(cs[nt][0], fsa * B.sx[nt][sj][0], acc[m][nt][0]);
+                    acc[m][nt][1] = fmaf(cs[nt][1], fsa * B.sx[nt][sj][1], acc[m][nt][1]);
+                    acc[m][nt][2] = fmaf(cs[nt][2], fsb * B.sx[nt][sj][0], acc[m][nt][2]);
+                    acc[m][nt][3] = fmaf(cs[nt][3], fsb * B.sx[nt][sj][1], acc[m][nt][3]);
+                }
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ float bf16r(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// SwiGLU of architecture.py:733-741 on bf16-rounded GEMM outputs
+__device__ __forceinline__ float swiglu(float gv, float uv, float limit) {
+    float gt = bf16r(gv), up = bf16r(uv);
+    if (limit > 0.f) {
+        up = fminf(fmaxf(up, -limit), limit);
+        gt = fminf(gt, limit);
+    }
+    const float silu = gt / (1.0f + expf(-gt));
+    return silu * up;
+}
+
+// Generic consumer loop.  `epi(it, red, tid)` runs on the 256 consumer
+// threads after the fixed-order cross-warp reduction inputs are in `red`.
+template <typename Decode, typename RowPtr, typename PreqScale, typename FP8Scale, typename Epi>
+__device__ void consume(const Smem &sm, int i0, int i1, int ue8m0, int *err, Decode decode,
+                        RowPtr rowptr, PreqScale preq_scale, FP8Scale f8s, Epi epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int g = lane >> 2, tig = lane & 3;
+    volatile int *abort = sm.flags();
+    float *red = sm.red();
+    BRegs B;
+    int key_src = -1, key_tok0 = -1, key_ntok = -1, key_a = -1;
+    int q = 0;
+    for (int i = i0; i < i1; ++i, ++q) {
+        const Item it = decode(i);
+        const int s = q % NSLOT;
+        if (it.bsrc != key_src || it.tok0 != key_tok0 || it.ntok != key_ntok || it.a != key_a) {
+            load_b(it, warp, lane, ue8m0, B, rowptr, preq_scale);
+            key_src = it.bsrc; key_tok0 = it.tok0; key_ntok = it.ntok; key_a = it.a;
+        }
+        bool ok = !*abort;
+        if (ok && !wf_wait(sm.full(s), (q / NSLOT) & 1, err)) { *abort = 1; ok = false; }
+        float acc[2][NTM][4];
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int nt = 0; nt < NTM; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[m][nt][c] = 0.f;
+        if (ok) compute_item(it, sm.slot(s), warp, lane, B, acc, f8s);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.empty(s));
+        // partials -> red[warp][arow][tok]
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int nt = 0; nt < NTM; ++nt) {
+                float *r0 = red + (warp * MAXR + 16 * m + g) * TPI + nt * 8 + 2 * tig;
+                float *r1 = r0 + 8 * TPI;
+                r0[0] = acc[m][nt][0]; r0[1] = acc[m][nt][1];
+                r1[0] = acc[m][nt][2]; r1[1] = acc[m][nt][3];
+            }
+        bar_sync(1, NCT);
+        epi(it, red, tid);
+        bar_sync(1, NCT);
+    }
+}
+
+__device__ __forceinline__ float red_sum(const float *red, int arow, int tok) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) v += red[(w * MAXR + arow) * TPI + tok];
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// router (K1, consumer warps): logits[t][e] = sum_k x[t][k] w[e][k] in fp64
+// ---------------------------------------------------------------------------
+__device__ void router_logits(const MoeArgs &a, const Smem &sm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int E = a.E, D = a.D, T = a.T;
+    const int G = gridDim.x;
+    static_assert(2 * 4 * TPI * 8 <= MISC_BYTES, "router partials must fit the misc buffer");
+    double *part = sm.misc();  // [2 rows][4 parts][TPI tokens]
+    const int nrows = (blockIdx.x < E) ? cdiv(E - blockIdx.x, G) : 0;
+    const int quarter = D / 4;
+    for (int p = 0; p < nrows; p += 2) {
+        for (int t0 = 0; t0 < T; t0 += TPI) {
+            const int rl = warp >> 2, pq = warp & 3;
+            const int r = p + rl;
+            const bool rv = r < nrows;
+            const int e = blockIdx.x + r * G;
+            double accd[TPI];
+#pragma unroll
+            for (int t = 0; t < TPI; ++t) accd[t] = 0.0;
+            if (rv) {
+                const __nv_bfloat16 *wrow = a.gate_w + (size_t)e * D + pq * quarter;
+                for (int k = lane * 8; k < quarter; k += 256) {
+                    const uint4 wu = ldg128(wrow + k);
+                    const uint32_t wv[4] = {wu.x, wu.y, wu.z, wu.w};
+                    float wf[8];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        wf[2 * c] = bf16_bits_to_f32(wv[c] & 0xffffu);
+                        wf[2 * c + 1] = bf16_bits_to_f32(wv[c] >> 16);
+                    }
+#pragma unroll
+                    for (int t = 0; t < TPI; ++t) {
+                        if (t0 + t < T) {
+                            const uint4 xu = ldg128(a.x + (size_t)(t0 + t) * D + pq * quarter + k);
+                            const uint32_t xv[4] = {xu.x, xu.y, xu.z, xu.w};
+                            double s = 0.0;
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                // bf16 x bf16 products are exact in fp32
+                                s += (double)(wf[2 * c] * bf16_bits_to_f32(xv[c] & 0xffffu));
+                                s += (double)(wf[2 * c + 1] * bf16_bits_to_f32(xv[c] >> 16));
+                            }
+                            accd[t] += s;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < TPI; ++t) {
+                double v = accd[t];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                accd[t] = v;
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < TPI; ++t) part[(rl * 4 + pq) * TPI + t] = accd[t];
+            }
+            bar_sync(1, NCT);
+            if (threadIdx.x < 2 * TPI) {
+                const int rl2 = threadIdx.x / TPI, t = threadIdx.x % TPI;
+                const int r2 = p + rl2;
+                if (r2 < nrows && t0 + t < T) {
+                    const double v = part[(rl2 * 4 + 0) * TPI + t] + part[(rl2 * 4 + 1) * TPI + t] +
+                                     part[(rl2 * 4 + 2) * TPI + t] + part[(rl2 * 4 + 3) * TPI + t];
+                    a.logits[(size_t)(t0 + t) * E + blockIdx.x + r2 * G] = (float)v;
+                }
+            }
+            bar_sync(1, NCT);
+        }
+    }
+}
+
+__device__ __forceinline__ void warp_argmax(float &v, int &idx) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    }
+}
+
+// Top-k and dispatch tables; run by the 256 consumer threads of one CTA.
+__device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int T = a.T, E = a.E, K = a.topk;
+    static_assert(2 * MAX_T * MAX_K * 2 <= RED_BYTES, "top-k tables must fit the reduction buffer");
+    static_assert(MAX_E * 4 <= MISC_BYTES, "expert counts must fit the misc buffer");
+    int16_t *ridx_s = reinterpret_cast<int16_t *>(sm.red());          // [T*K]
+    int16_t *pof_s = ridx_s + MAX_T * MAX_K;                            // [T*K]
+    int *cnt_s = reinterpret_cast<int *>(sm.misc());                    // [El]
+    for (int t = warp; t < T; t += NCW) {
+        float sc[MAX_E / 32], bs[MAX_E / 32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < MAX_E / 32; ++i) {
+            const int e = lane + 32 * i;
+            const float l = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+            sc[i] = l;
+            mx = fmaxf(mx, l);
+        }
+        if (a.score_func == WF_SCORE_SOFTMAX) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < MAX_E / 32; ++i) {
+                const int e = lane + 32 * i;
+                sc[i] = e < E ? expf(sc[i] - mx) : 0.f;
+                sum += sc[i];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+            for (int i = 0; i < MAX_E / 32; ++i) sc[i] = sc[i] / sum;
+        } else if (a.score_func == WF_SCORE_SIGMOID) {
+#pragma unroll
+            for (int i = 0; i < MAX_E / 32; ++i) sc[i] = 1.0f / (1.0f + expf(-sc[i]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < MAX_E / 32; ++i) {
+                const float l = sc[i];
+                sc[i] = sqrtf(l > 20.f ? l : log1pf(expf(l)));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < MAX_E / 32; ++i) {
+            const int e = lane + 32 * i;
+            bs[i] = e < E ? (a.gate_b ? sc[i] + __ldg(a.gate_b + e) : sc[i]) : -INFINITY;
+        }
+        int sel[MAX_K];
+        if (a.hash) {
+            long long id = __ldg(a.ids + t);
+            if (id < 0 || id >= a.vocab) { if (lane == 0) atomicOr(a.err, kErrExpertId); id = 0; }
+            for (int j = 0; j < K; ++j) {
+                int e = __ldg(a.tid2eid + id * K + j);
+                if (e < 0 || e >= E) { if (lane == 0) atomicOr(a.err, kErrExpertId); e = 0; }
+                sel[j] = e;
+            }
+        } else {
+            for (int j = 0; j < K; ++j) {
+                float bv = -INFINITY; int bi = 0x7fffffff;
+#pragma unroll
+                for (int i = 0; i < MAX_E / 32; ++i) {
+                    const int e = lane + 32 * i;
+                    if (e < E && (bs[i] > bv || (bs[i] == bv && e < bi))) { bv = bs[i]; bi = e; }
+                }
+                warp_argmax(bv, bi);
+                sel[j] = bi;
+#pragma unroll
+                for (int i = 0; i < MAX_E / 32; ++i)
+                    if (lane + 32 * i == bi) bs[i] = -INFINITY;
+            }
+        }
+        float wsel[MAX_K];
+        float wsum = 0.f;
+        for (int j = 0; j < K; ++j) {
+            const int e = sel[j];
+            float v = 0.f;
+#pragma unroll
+            for (int i = 0; i < MAX_E / 32; ++i)
+                if (i == (e >> 5)) v = sc[i];
+            v = __shfl_sync(0xffffffffu, v, e & 31);
+            wsel[j] = v;
+            wsum += v;
+        }
+        if (lane == 0) {
+            for (int j = 0; j < K; ++j) {
+                float w = wsel[j];
+                if (a.score_func != WF_SCORE_SOFTMAX) w = w / wsum;
+                w = w * a.route_scale;
+                a.rw[t * K + j] = w;
+                ridx_s[t * K + j] = (int16_t)sel[j];
+                pof_s[t * K + j] = -1;
+                if (a.out_w) a.out_w[(size_t)t * K + j] = w;
+                if (a.out_idx) a.out_idx[(size_t)t * K + j] = sel[j];
+            }
+        }
+    }
+    __threadfence();
+    bar_sync(1, NCT);
+    if (a.route_only) return;
+    // per local expert: number of tokens that keep it (a duplicate keeps its last slot)
+    for (int el = tid; el < a.El; el += NCT) {
+        const int e = a.e0 + el;
+        int c = 0;
+        for (int t = 0; t < T; ++t)
+            for (int j = 0; j < K; ++j) {
+                if (ridx_s[t * K + j] != e) continue;
+                bool later = false;
+                for (int j2 = j + 1; j2 < K; ++j2) later |= ridx_s[t * K + j2] == e;
+                c += !later;
+            }
+        cnt_s[el] = c;
+    }
+    bar_sync(1, NCT);
+    if (tid == 0) {
+        int n = 0, off = 0, it2 = 0, it3 = 0, tgt = 0;
+        const int per2 = a.I / a.g.nh13, per3 = a.D / a.g.r2;
+        for (int el = 0; el < a.El; ++el) {
+            const int c = cnt_s[el];
+            if (c) {
+                const int TG = cdiv(c, TPI);
+                a.act_expert[n] = a.e0 + el; a.act_off[n] = off;
+                a.act_it2[n] = it2; a.act_it3[n] = it3;
+                it2 += per2 * TG; it3 += per3 * TG; tgt += TG; off += c;
+                cnt_s[el] = n++;
+            } else {
+                cnt_s[el] = -1;
+            }
+        }
+        a.act_off[n] = off; a.act_it2[n] = it2; a.act_it3[n] = it3;
+        a.hdr[H_NACT] = n; a.hdr[H_IT2] = it2; a.hdr[H_IT3] = it3; a.hdr[H_TGT] = tgt;
+        a.hdr[H_NPAIR] = off;
+    }
+    bar_sync(1, NCT);
+    for (int el = tid; el < a.El; el += NCT) {
+        const int ai = cnt_s[el];
+        if (ai < 0) continue;
+        const int e = a.e0 + el;
+        int p = a.act_off[ai];
+        for (int t = 0; t < T; ++t)
+            for (int j = 0; j < K; ++j) {
+                if (ridx_s[t * K + j] != e) continue;
+                bool later = false;
+                for (int j2 = j + 1; j2 < K; ++j2) later |= ridx_s[t * K + j2] == e;
+                if (later) continue;
+                a.pair_tok[p] = t;
+                a.pair_w[p] = __ldcg(a.rw + t * K + j);
+                pof_s[t * K + j] = (int16_t)p;
+                ++p;
+            }
+    }
+    bar_sync(1, NCT);
+    for (int t = tid; t < T; t += NCT) {
+        int ee[MAX_K], pp[MAX_K], n = 0;
+        for (int j = 0; j < K; ++j) {
+            const int p = pof_s[t * K + j];
+            if (p < 0) continue;
+            const int e = ridx_s[t * K + j];
+            int m = n++;
+            while (m > 0 && ee[m - 1] > e) { ee[m] = ee[m - 1]; pp[m] = pp[m - 1]; --m; }
+            ee[m] = e; pp[m] = p;
+        }
+        for (int m = 0; m < n; ++m) a.tok_pairs[t * K + m] = pp[m];
+        a.tok_np[t] = n;
+    }
+    __threadfence();
+}
+
+// ---------------------------------------------------------------------------
+// combine of one output row block (K3): ascending-expert fp32 sum + shared
+// ---------------------------------------------------------------------------
+__device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
+    const int T = a.T, D = a.D, K = a.topk;
+    const unsigned short *o = reinterpret_cast<const unsigned short *>(a.o);
+    const unsigned short *os = reinterpret_cast<const unsigned short *>(a.os);
+    for (int idx = threadIdx.x; idx < T * nrows; idx += NCT) {
+        const int t = idx / nrows, r = row0 + idx % nrows;
+        float acc = 0.f;
+        const int np = __ldcg(a.tok_np + t);
+        for (int qq = 0; qq < np; ++qq) {
+            const int p = __ldcg(a.tok_pairs + t * K + qq);
+            acc += bf16_bits_to_f32(__ldcg(o + (size_t)p * D + r));
+        }
+        if (a.partial) {
+            a.y_partial[(size_t)t * D + r] = acc;
+        } else {
+            acc += bf16_bits_to_f32(__ldcg(os + (size_t)t * D + r));
+            a.y[(size_t)t * D + r] = __float2bfloat16_rn(acc);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void init_smem(const Smem &sm) {
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSLOT; ++s) {
+            mbar_init(sm.full(s), 1);
+            mbar_init(sm.empty(s), NCW);
+        }
+        sm.flags()[0] = 0;  // abort
+        sm.flags()[1] = 0;  // scratch flag
+        fence_mbar_init();
+    }
+    __syncthreads();
+}
+
+struct MoeRowPtr {
+    const MoeArgs *a;
+    __device__ const void *operator()(const Item &it, int j) const {
+        const int p = it.tok0 + j;
+        switch (it.bsrc) {
+            case BS_XPAIR: return a->x + (size_t)__ldg(a->pair_tok + p) * a->D;
+            case BS_XTOK: return a->x + (size_t)p * a->D;
+            case BS_H: return a->h + (size_t)p * a->I;
+            default: return a->hs + (size_t)p * a->I;
+        }
+    }
+};
+
+struct NoPreq {
+    __device__ float operator()(const Item &, int, int) const { return 0.f; }
+};
+
+__global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem sm{smem_raw};
+    init_smem(sm);
+    const int n = a.route_only ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
+    int i0, i1;
+    item_range(n, i0, i1);
+    auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0); };
+    if ((threadIdx.x >> 5) == NCW) {
+        produce(sm, i0, i1, a.err, decode);
+        return;
+    }
+    router_logits(a, sm);
+    __threadfence();
+    bar_sync(1, NCT);
+    const unsigned nrc = min((unsigned)a.E, gridDim.x);
+    if (blockIdx.x < nrc) {
+        if (threadIdx.x == 0) {
+            const unsigned old = atomicAdd(a.cnt_router, 1u);
+            sm.flags()[1] = (old == nrc - 1);
+        }
+        bar_sync(1, NCT);
+        if (sm.flags()[1]) {
+            __threadfence();
+            topk_dispatch(a, sm);
+            if (threadIdx.x == 0) *a.cnt_router = 0u;
+        }
+        bar_sync(1, NCT);
+    }
+    MoeRowPtr rp{&a};
+    auto f8 = [&](int rblk, int kb) {
+        const int kbs = a.D / 128;
+        if (a.shared_f32) return __ldg((const float *)a.ss13 + rblk * kbs + kb);
+        return e8m0_to_f32(__ldg((const uint8_t *)a.ss13 + rblk * kbs + kb));
+    };
+    auto epi = [&](const Item &it, const float *red, int tid) {
+        const int nh = it.rrows;
+        for (int idx = tid; idx < nh * it.ntok; idx += NCT) {
+            const int tok = idx / nh, j = idx % nh;
+            const float hv = swiglu(red_sum(red, j, tok), red_sum(red, nh + j, tok), a.swiglu_limit);
+            a.hs[(size_t)(it.tok0 + tok) * a.I + it.row0 + j] = __float2bfloat16_rn(hv);
+        }
+    };
+    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+}
+
+__global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ MoeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem sm{smem_raw};
+    init_smem(sm);
+    const int n_act = a.hdr[H_NACT], n_it2 = a.hdr[H_IT2];
+    const int n = n_it2 + (a.D / a.g.rs2) * cdiv(a.T, TPI);
+    int i0, i1;
+    item_range(n, i0, i1);
+    auto decode = [&](int i) { return decode_moe(KID_MID, a, i, n_act, n_it2); };
+    if ((threadIdx.x >> 5) == NCW) {
+        produce(sm, i0, i1, a.err, decode);
+        return;
+    }
+    MoeRowPtr rp{&a};
+    auto f8 = [&](int rblk, int kb) {
+        const int kbs = a.I / 128;
+        if (a.shared_f32) return __ldg((const float *)a.ss2 + rblk * kbs + kb);
+        return e8m0_to_f32(__ldg((const uint8_t *)a.ss2 + rblk * kbs + kb));
+    };
+    auto epi = [&](const Item &it, const float *red, int tid) {
+        if (it.ep == EP_RSWIGLU) {
+            const int nh = it.rrows;
+            for (int idx = tid; idx < nh * it.ntok; idx += NCT) {
+                const int tok = idx / nh, j = idx % nh;
+                const int p = it.tok0 + tok;
+                float hv = swiglu(red_sum(red, j, tok), red_sum(red, nh + j, tok), a.swiglu_limit);
+                hv = __ldg(a.pair_w + p) * hv;
+                a.h[(size_t)p * a.I + it.row0 + j] = __float2bfloat16_rn(hv);
+            }
+        } else {
+            const int nr = it.rrows;
+            for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
+                const int tok = idx / nr, r = idx % nr;
+                a.os[(size_t)(it.tok0 + tok) * a.D + it.row0 + r] =
+                    __float2bfloat16_rn(red_sum(red, r, tok));
+            }
+        }
+    };
+    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+}
+
+__global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ MoeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem sm{smem_raw};
+    init_smem(sm);
+    const int n_act = a.hdr[H_NACT], n = a.hdr[H_IT3], tgt = a.hdr[H_TGT];
+    if (n_act == 0) {  // no local expert has tokens: y = shared part only
+        if ((threadIdx.x >> 5) == NCW) return;
+        const int nrb = a.D / a.g.r2;
+        for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x) combine_rows(a, rb * a.g.r2, a.g.r2);
+        return;
+    }
+    int i0, i1;
+    item_range(n, i0, i1);
+    auto decode = [&](int i) { return decode_moe(KID_DOWN, a, i, n_act, 0); };
+    if ((threadIdx.x >> 5) == NCW) {
+        produce(sm, i0, i1, a.err, decode);
+        return;
+    }
+    MoeRowPtr rp{&a};
+    auto f8 = [&](int, int) { return 0.f; };
+    volatile int *flag = sm.flags() + 1;
+    auto epi = [&](const Item &it, const float *red, int tid) {
+        const int nr = it.rrows;
+        for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
+            const int tok = idx / nr, r = idx % nr;
+            a.o[(size_t)(it.tok0 + tok) * a.D + it.row0 + r] = __float2bfloat16_rn(red_sum(red, r, tok));
+        }
+        __threadfence();
+        bar_sync(1, NCT);
+        if (tid == 0) {
+            const unsigned old = atomicAdd(a.cnt_rb + it.rb, 1u);
+            *flag = (old == (unsigned)tgt - 1);
+        }
+        bar_sync(1, NCT);
+        if (*flag) {
+            __threadfence();
+            combine_rows(a, it.row0, nr);
+            if (tid == 0) a.cnt_rb[it.rb] = 0u;
+        }
+    };
+    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+}
+
+__global__ void k_moe_finish(const float *yp, const __nv_bfloat16 *os, __nv_bfloat16 *y, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(yp[i] + __bfloat162float(os[i]));
+}
+
+__global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ DenseArgs d) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem sm{smem_raw};
+    init_smem(sm);
+    const int n = (d.N / d.rows) * (d.G > 0 ? d.G : cdiv(d.M, TPI));
+    int i0, i1;
+    item_range(n, i0, i1);
+    auto decode = [&](int i) { return decode_dense(d, i); };
+    if ((threadIdx.x >> 5) == NCW) {
+        produce(sm, i0, i1, d.err, decode);
+        return;
+    }
+    auto rowptr = [&](const Item &it, int j) -> const void * {
+        return d.a + (size_t)(it.tok0 + j) * d.K;
+    };
+    auto preq = [&](const Item &it, int j, int s) {
+        const size_t ix = (size_t)(it.tok0 + j) * (d.K / 128) + s;
+        return d.a_f32 ? __ldg((const float *)d.a_s + ix) : e8m0_to_f32(__ldg((const uint8_t *)d.a_s + ix));
+    };
+    auto f8 = [&](int rblk, int kb) {
+        const size_t ix = (size_t)rblk * (d.K / 128) + kb;
+        return d.b_f32 ? __ldg((const float *)d.b_s + ix) : e8m0_to_f32(__ldg((const uint8_t *)d.b_s + ix));
+    };
+    auto epi = [&](const Item &it, const float *red, int tid) {
+        const int nr = it.rrows;
+        for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
+            const int tok = idx / nr, r = idx % nr;
+            d.out[(size_t)(it.tok0 + tok) * d.N + it.row0 + r] = __float2bfloat16_rn(red_sum(red, r, tok));
+        }
+    };
+    consume(sm, i0, i1, 1, d.err, decode, rowptr, preq, f8, epi);
+}
+
+// ---- standalone quantizers --------------------------------------------------
+// act_quant: one warp per (row, 128-block); lane handles 4 elements.
+__global__ void k_act_quant(const __nv_bfloat16 *x, long long M, long long K, int block,
+                            int ue8m0, uint8_t *q, void *s, int s_f32) {
+    const long long nb = K / block;
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= M * nb) return;
+    const long long row = wid / nb, b = wid % nb;
+    const __nv_bfloat16 *src = x + row * K + b * block;
+    float amax = 0.f;
+    for (int e = lane; e < block; e += 32) amax = fmaxf(amax, fabsf(__bfloat162float(src[e])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = round_scale_e8(fmaxf(amax, 1e-4f), ue8m0);
+    for (int e = lane; e < block; e += 32) {
+        float v = __bfloat162float(src[e]);
+        v = ue8m0 ? v * (1.0f / sc) : __fdiv_rn(v, sc);
+        v = fminf(fmaxf(v, -448.f), 448.f);
+        q[row * K + b * block + e] = (uint8_t)(f32x2_to_e4m3x2(v, 0.f) & 0xff);
+    }
+    if (lane == 0) {
+        if (s_f32) ((float *)s)[row * nb + b] = sc;
+        else ((uint8_t *)s)[row * nb + b] = (uint8_t)((__float_as_uint(sc) >> 23) & 0xff);
+    }
+}
+
+// fp4_act_quant: one thread per 32-block.  E2M1 code of |q| by the midpoint
+// table with ties to the even code (torch_ops.py:52-58).
+__device__ __forceinline__ uint32_t e2m1_code(float a) {
+    const float mid[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+    int lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 7; ++i) { lo += mid[i] < a; hi += mid[i] <= a; }
+    return (uint32_t)(lo + ((hi != lo) && (lo & 1)));
+}
+
+__global__ void k_fp4_act_quant(const __nv_bfloat16 *x, long long M, long long K, uint8_t *q,
+                                uint8_t *s) {
+    const long long nb = K / 32;
+    const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= M * nb) return;
+    const long long row = id / nb, b = id % nb;
+    const __nv_bfloat16 *src = x + row * K + b * 32;
+    float v[32];
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) { v[e] = __bfloat162float(src[e]); amax = fmaxf(amax, fabsf(v[e])); }
+    amax = fmaxf(amax, 6.0f * 1.1754943508222875e-38f);
+    const float x6 = amax * (1.0f / 6.0f);
+    const uint32_t bits = __float_as_uint(x6);
+    const float sc = (bits & 0x7fffffu) ? __uint_as_float(((bits >> 23) + 1) << 23) : x6;
+    uint8_t *dst = q + row * (K / 2) + b * 16;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        float q0 = fminf(fmaxf(v[2 * e] / sc, -6.f), 6.f);
+        float q1 = fminf(fmaxf(v[2 * e + 1] / sc, -6.f), 6.f);
+        uint32_t c0 = e2m1_code(fabsf(q0)) | (q0 < 0.f ? 8u : 0u);
+        uint32_t c1 = e2m1_code(fabsf(q1)) | (q1 < 0.f ? 8u : 0u);
+        dst[e] = (uint8_t)(c0 | (c1 << 4));
+    }
+    s[row * nb + b] = (uint8_t)((__float_as_uint(sc) >> 23) & 0xff);
+}
+
+__global__ void k_scale_range(const uint8_t *s, long long n, int *bad) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint8_t b = s[i];
+        if (b < 104 || b > 140) { atomicOr(bad, 1); return; }
+    }
+}
+
+}  // namespace wf
+
+// =============================================================================
+// host side: C ABI
+// =============================================================================
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return WF_E_CUDA;
+}
+
+struct DevInfo {
+    int sms = 0;
+    bool attr_done = false;
+};
+thread_local DevInfo g_dev[64];
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    DevInfo &d = g_dev[dev];
+    if (!d.sms) cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    return d.sms;
+}
+
+int ensure_attrs() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return WF_E_CUDA;
+    DevInfo &d = g_dev[dev];
+    if (d.attr_done) return WF_OK;
+    const void *ks[] = {(const void *)wf::k_moe_up, (const void *)wf::k_moe_mid,
+                        (const void *)wf::k_moe_down, (const void *)wf::k_dense};
+    for (const void *k : ks) {
+        cudaError_t e =
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, wf::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    }
+    d.attr_done = true;
+    return WF_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// smem row stride: row bytes rounded up to 128, plus 64 (FP4) or 16 (FP8) so
+// that the consumer warps' 16-byte loads of 8 rows fall in distinct banks
+int stride_fp4(int K) { return ((K / 2 + 127) / 128) * 128 + 64; }
+int stride_fp8(int K) { return ((K + 127) / 128) * 128 + 16; }
+
+int rows_fit(int stride) {
+    int r = wf::SLOT_W / stride;
+    return r > wf::MAXR ? wf::MAXR : r;
+}
+
+struct WsLayout {
+    size_t logits, hdr, act_expert, act_off, act_it2, act_it3, pair_tok, pair_w, tok_np,
+        tok_pairs, ridx, rw, h, hs, o, os, cnt_router, cnt_rb, err, total;
+};
+
+WsLayout ws_layout(const wf_moe_config *c) {
+    WsLayout L{};
+    size_t off = 0;
+    const size_t T = c->max_tokens, K = c->topk, E = c->n_experts, El = c->n_local_experts;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    L.err = take(16);
+    L.cnt_router = take(16);
+    L.cnt_rb = take((size_t)(c->dim / 8 + 1) * 4);
+    L.hdr = take(wf::H_SIZE * 4);
+    L.logits = take(T * E * 4);
+    L.act_expert = take((El + 1) * 4);
+    L.act_off = take((El + 1) * 4);
+    L.act_it2 = take((El + 1) * 4);
+    L.act_it3 = take((El + 1) * 4);
+    L.pair_tok = take(T * K * 4);
+    L.pair_w = take(T * K * 4);
+    L.tok_np = take(T * 4);
+    L.tok_pairs = take(T * K * 4);
+    L.ridx = take(T * K * 4);
+    L.rw = take(T * K * 4);
+    L.h = take(T * K * c->inter_dim * 2);
+    L.hs = take(T * c->inter_dim * 2);
+    L.o = take(T * K * c->dim * 2);
+    L.os = take(T * c->dim * 2);
+    L.total = off;
+    return L;
+}
+
+int check_cfg(const wf_moe_config *c) {
+    if (!c) return fail(WF_E_ARG, "null config");
+    const int D = c->dim, I = c->inter_dim;
+    if (D <= 0 || I <= 0 || D % 128 || I % 128 || D > wf::KMAX || I > wf::KMAX)
+        return fail(WF_E_SHAPE, "dim and inter_dim must be positive multiples of 128, at most 4096");
+    if (c->n_experts <= 0 || c->n_experts > wf::MAX_E)
+        return fail(WF_E_SHAPE, "n_experts must be in 1..512");
+    if (c->n_local_experts <= 0 || c->expert_offset < 0 ||
+        c->expert_offset + c->n_local_experts > c->n_experts)
+        return fail(WF_E_SHAPE, "local expert range outside [0, n_experts)");
+    if (c->topk <= 0 || c->topk > wf::MAX_K || c->topk > c->n_experts)
+        return fail(WF_E_SHAPE, "topk must be in 1..min(8, n_experts)");
+    if (c->score_func < 0 || c->score_func > 2) return fail(WF_E_DTYPE, "bad score_func");
+    if (c->max_tokens <= 0 || c->max_tokens > wf::MAX_T)
+        return fail(WF_E_SHAPE, "max_tokens must be in 1..256");
+    if (c->hash_layer && c->vocab <= 0) return fail(WF_E_SHAPE, "hash layer needs vocab > 0");
+    return WF_OK;
+}
+
+wf::Geo make_geo(int D, int I) {
+    wf::Geo g;
+    g.st_w13 = stride_fp4(D);
+    g.st_w2 = stride_fp4(I);
+    g.st_s13 = stride_fp8(D);
+    g.st_s2 = stride_fp8(I);
+    auto pick_h = [&](int stride) {  // h-rows per SwiGLU item: 2*nh rows, nh | I
+        int r = rows_fit(stride) / 2;
+        int nh = r >= 16 ? 16 : r >= 8 ? 8 : 4;
+        while (I % nh) nh /= 2;
+        return nh;
+    };
+    auto pick_r = [&](int stride) {  // rows per plain item: 32, 16 or 8, divides D
+        const int fit = rows_fit(stride);
+        int r = fit >= 32 ? 32 : fit >= 16 ? 16 : 8;
+        while (D % r) r /= 2;
+        return r;
+    };
+    g.nh13 = pick_h(g.st_w13);
+    g.nhs13 = pick_h(g.st_s13);
+    g.r2 = pick_r(g.st_w2);
+    g.rs2 = pick_r(g.st_s2);
+    return g;
+}
+
+int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
+              const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a) {
+    int rc = check_cfg(c);
+    if (rc) return rc;
+    if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
+    if (T <= 0 || T > c->max_tokens) return fail(WF_E_SHAPE, "T outside 1..max_tokens");
+    const WsLayout L = ws_layout(c);
+    if (ws_bytes < L.total) return fail(WF_E_ARG, "workspace too small");
+    if (!w->gate_w) return fail(WF_E_ARG, "null gate weight");
+    if (c->hash_layer && (!w->tid2eid || !ids)) return fail(WF_E_ARG, "hash layer needs tid2eid and input_ids");
+    memset(&a, 0, sizeof(a));
+    a.T = T; a.D = c->dim; a.I = c->inter_dim; a.E = c->n_experts; a.El = c->n_local_experts;
+    a.e0 = c->expert_offset; a.topk = c->topk; a.score_func = c->score_func;
+    a.hash = c->hash_layer; a.ue8m0 = c->ue8m0; a.vocab = c->vocab;
+    a.route_scale = c->route_scale; a.swiglu_limit = c->swiglu_limit;
+    a.x = (const __nv_bfloat16 *)x; a.ids = (const long long *)ids;
+    a.gate_w = (const __nv_bfloat16 *)w->gate_w; a.gate_b = c->hash_layer ? nullptr : w->gate_bias;
+    a.tid2eid = w->tid2eid;
+    a.w13 = w->w13; a.w13_s = w->w13_s; a.w2 = w->w2; a.w2_s = w->w2_s;
+    a.sw13 = w->shared_w13; a.sw2 = w->shared_w2; a.ss13 = w->shared_s13; a.ss2 = w->shared_s2;
+    a.shared_f32 = w->shared_scale_kind == WF_SCALE_F32;
+    uint8_t *b = (uint8_t *)ws;
+    a.logits = (float *)(b + L.logits);
+    a.hdr = (int *)(b + L.hdr);
+    a.act_expert = (int *)(b + L.act_expert);
+    a.act_off = (int *)(b + L.act_off);
+    a.act_it2 = (int *)(b + L.act_it2);
+    a.act_it3 = (int *)(b + L.act_it3);
+    a.pair_tok = (int *)(b + L.pair_tok);
+    a.pair_w = (float *)(b + L.pair_w);
+    a.tok_np = (int *)(b + L.tok_np);
+    a.tok_pairs = (int *)(b + L.tok_pairs);
+    a.ridx = (int *)(b + L.ridx);
+    a.rw = (float *)(b + L.rw);
+    a.h = (__nv_bfloat16 *)(b + L.h);
+    a.hs = (__nv_bfloat16 *)(b + L.hs);
+    a.o = (__nv_bfloat16 *)(b + L.o);
+    a.os = (__nv_bfloat16 *)(b + L.os);
+    a.cnt_router = (unsigned *)(b + L.cnt_router);
+    a.cnt_rb = (unsigned *)(b + L.cnt_rb);
+    a.err = (int *)(b + L.err);
+    a.g = make_geo(a.D, a.I);
+    return WF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *wf_last_error(void) { return g_err.c_str(); }
+
+int wf_device_sm_count(void) { return sm_count(); }
+
+size_t wf_moe_workspace_bytes(const wf_moe_config *cfg) {
+    if (check_cfg(cfg)) return 0;
+    return ws_layout(cfg).total;
+}
+
+static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
+                      void *const *ev = nullptr) {
+    int rc = ensure_attrs();
+    if (rc) return rc;
+    const int G = sm_count();
+    if (G <= 0) return fail(WF_E_CUDA, "no CUDA device");
+    a.route_only = route_only;
+    if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[0], st, cudaEventRecordExternal);
+    wf::k_moe_up<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
+    if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[1], st, cudaEventRecordExternal);
+    if (!route_only) {
+        wf::k_moe_mid<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
+        if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[2], st, cudaEventRecordExternal);
+        wf::k_moe_down<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
+        if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[3], st, cudaEventRecordExternal);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "MoE kernel launch");
+    return WF_OK;
+}
+
+int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                   const int64_t *input_ids, int32_t T, void *y, float *y_partial,
+                   float *out_weights, int64_t *out_indices, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+    wf::MoeArgs a;
+    int rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a);
+    if (rc) return rc;
+    if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
+    if (!w->w13 || !w->w13_s || !w->w2 || !w->w2_s || !w->shared_w13 || !w->shared_s13 ||
+        !w->shared_w2 || !w->shared_s2)
+        return fail(WF_E_ARG, "null expert weight pointer");
+    a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
+    a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    return launch_moe(a, false, (cudaStream_t)stream);
+}
+
+int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                         const int64_t *input_ids, int32_t T, void *y, float *y_partial,
+                         float *out_weights, int64_t *out_indices, void *workspace,
+                         size_t workspace_bytes, void *stream, void *const *events) {
+    if (!events) return fail(WF_E_ARG, "null events");
+    for (int i = 0; i < 4; ++i)
+        if (!events[i]) return fail(WF_E_ARG, "null event");
+    wf::MoeArgs a;
+    int rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a);
+    if (rc) return rc;
+    if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
+    a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
+    a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    return launch_moe(a, false, (cudaStream_t)stream, events);
+}
+
+int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                 const int64_t *input_ids, int32_t T, float *out_weights, int64_t *out_indices,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+    wf::MoeArgs a;
+    int rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a);
+    if (rc) return rc;
+    if (!out_weights || !out_indices) return fail(WF_E_ARG, "null router outputs");
+    a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    return launch_moe(a, true, (cudaStream_t)stream);
+}
+
+int wf_moe_finish(const wf_moe_config *cfg, const float *yp, int32_t T, int32_t row0, void *y,
+                  const void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (!yp || !y || !workspace) return fail(WF_E_ARG, "null pointer");
+    const WsLayout L = ws_layout(cfg);
+    if (workspace_bytes < L.total) return fail(WF_E_ARG, "workspace too small");
+    if (T <= 0 || row0 < 0 || row0 + T > cfg->max_tokens)
+        return fail(WF_E_SHAPE, "rows row0..row0+T outside 0..max_tokens");
+    const int n = T * cfg->dim;
+    const __nv_bfloat16 *os =
+        (const __nv_bfloat16 *)((const uint8_t *)workspace + L.os) + (size_t)row0 * cfg->dim;
+    wf::k_moe_finish<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(yp, os, (__nv_bfloat16 *)y, n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "finish launch");
+}
+
+int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream) {
+    if (!workspace || workspace_bytes < 16) return fail(WF_E_ARG, "null workspace");
+    int host = 0;
+    cudaError_t e = cudaMemcpyAsync(&host, workspace, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "read error word");
+    if (host & wf::kErrTimeout) return fail(WF_E_TIMEOUT, "a device wait timed out");
+    if (host & wf::kErrExpertId) return fail(WF_E_EXPERT_ID, "token or expert id out of range");
+    return WF_OK;
+}
+
+int wf_act_quant(const void *x, int64_t M, int64_t K, int32_t block, int32_t ue8m0, void *q,
+                 void *s, int32_t scale_kind, void *stream) {
+    if (!x || !q || !s) return fail(WF_E_ARG, "null pointer");
+    if (M <= 0 || K <= 0 || block <= 0 || K % block) return fail(WF_E_SHAPE, "K must be a multiple of block");
+    if (scale_kind != WF_SCALE_F32 && scale_kind != WF_SCALE_E8M0) return fail(WF_E_DTYPE, "bad scale kind");
+    if (scale_kind == WF_SCALE_E8M0 && !ue8m0) return fail(WF_E_DTYPE, "e8m0 scales need ue8m0 rounding");
+    const long long warps = M * (K / block);
+    const long long blocks = (warps * 32 + 255) / 256;
+    wf::k_act_quant<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16 *)x, M, K, block, ue8m0, (uint8_t *)q, s, scale_kind == WF_SCALE_F32);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "act_quant launch");
+}
+
+int wf_fp4_act_quant(const void *x, int64_t M, int64_t K, void *q, void *s, void *stream) {
+    if (!x || !q || !s) return fail(WF_E_ARG, "null pointer");
+    if (M <= 0 || K <= 0 || K % 32) return fail(WF_E_SHAPE, "K must be a multiple of 32");
+    const long long n = M * (K / 32);
+    wf::k_fp4_act_quant<<<(unsigned)((n + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16 *)x, M, K, (uint8_t *)q, (uint8_t *)s);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "fp4_act_quant launch");
+}
+
+size_t wf_gemm_workspace_bytes(int64_t, int64_t, int64_t) { return 256; }
+
+static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const void *b,
+                 const void *b_s, int b_kind, int64_t M, int64_t N, int64_t K, int64_t G,
+                 void *out, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!a || !a_s || !b || !b_s || !out) return fail(WF_E_ARG, "null pointer");
+    if (!ws || ws_bytes < 16) return fail(WF_E_ARG, "workspace too small");
+    if (M <= 0 || N <= 0 || K <= 0 || K % 128 || K > wf::KMAX || N % 8)
+        return fail(WF_E_SHAPE, "need K a multiple of 128 (<= 4096) and N a multiple of 8");
+    if ((a_kind != WF_SCALE_F32 && a_kind != WF_SCALE_E8M0) ||
+        (b_kind != WF_SCALE_F32 && b_kind != WF_SCALE_E8M0))
+        return fail(WF_E_DTYPE, "bad scale kind");
+    if (M > (1 << 30) || N > (1 << 30) || G > (1 << 20)) return fail(WF_E_SHAPE, "too large");
+    int rc = ensure_attrs();
+    if (rc) return rc;
+    wf::DenseArgs d;
+    d.M = (int)M; d.N = (int)N; d.K = (int)K; d.G = (int)G;
+    d.wfmt = wfmt; d.a_f32 = a_kind == WF_SCALE_F32; d.b_f32 = b_kind == WF_SCALE_F32;
+    d.a = (const uint8_t *)a; d.a_s = a_s; d.b = (const uint8_t *)b; d.b_s = b_s;
+    d.out = (__nv_bfloat16 *)out; d.err = (int *)ws;
+    d.stride = wfmt == wf::FMT_FP4 ? stride_fp4((int)K) : stride_fp8((int)K);
+    const int fit = rows_fit(d.stride);
+    d.rows = (fit >= 32 && N % 32 == 0) ? 32 : (fit >= 16 && N % 16 == 0) ? 16 : 8;
+    const int G_ = sm_count();
+    wf::k_dense<<<G_, wf::NTHR, wf::SMEM_BYTES, st>>>(d);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "gemm launch");
+}
+
+int wf_fp8_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *b,
+                const void *b_s, int32_t b_scale_kind, int64_t M, int64_t N, int64_t K, void *out,
+                void *workspace, size_t workspace_bytes, void *stream) {
+    return dense(wf::FMT_FP8, a, a_s, a_scale_kind, b, b_s, b_scale_kind, M, N, K, 0, out,
+                 workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int wf_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *b,
+                const void *b_s, int64_t M, int64_t N, int64_t K, void *out, void *workspace,
+                size_t workspace_bytes, void *stream) {
+    return dense(wf::FMT_FP4, a, a_s, a_scale_kind, b, b_s, WF_SCALE_E8M0, M, N, K, 0, out,
+                 workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int wf_grouped_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, const void *w,
+                        const void *w_s, int64_t G, int64_t N, int64_t K, void *out,
+                        void *workspace, size_t workspace_bytes, void *stream) {
+    if (G <= 0) return fail(WF_E_SHAPE, "G must be positive");
+    return dense(wf::FMT_FP4, a, a_s, a_scale_kind, w, w_s, WF_SCALE_E8M0, G, N, K, G, out,
+                 workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int wf_fp4_scales_in_range(const uint8_t *scales, int64_t n, void *stream) {
+    if (!scales || n < 0) return fail(WF_E_ARG, "null scales");
+    int *dbad = nullptr;
+    // load-time check: a 4-byte flag through the stream-ordered allocator
+    cudaError_t e = cudaMallocAsync((void **)&dbad, 4, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync");
+    int host = 0;
+    e = cudaMemsetAsync(dbad, 0, 4, (cudaStream_t)stream);
+    if (e == cudaSuccess && n > 0) {
+        wf::k_scale_range<<<296, 256, 0, (cudaStream_t)stream>>>(scales, n, dbad);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&host, dbad, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    cudaFreeAsync(dbad, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scale range check");
+    return host ? 0 : 1;
+}
+
+}  // extern "C"
