@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--sweep", default="1,4,16", help="extra token counts measured at N=1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--init", default="quant", choices=("quant", "random"),
+                    help="quant: N(0,0.02) weights through the FP4 quantizer; random: random FP4 bytes "
+                         "with typical scales (fewer launches, for profiler captures)")
     return ap.parse_args()
 
 
@@ -141,7 +144,7 @@ def fp8_block_quant_torch(w):
     return q.reshape(n, k).view(torch.uint8), scale.to(torch.float8_e8m0fnu).view(torch.uint8)
 
 
-def make_layer(seed, rank, world, max_tokens, device):
+def make_layer(seed, rank, world, max_tokens, device, init="quant"):
     import torch
 
     from wanferenz_b200 import ops
@@ -160,7 +163,11 @@ def make_layer(seed, rank, world, max_tokens, device):
     w13_s = torch.empty(El, 2 * I, D // 32, dtype=torch.uint8, device=device)
     w2 = torch.empty(El, D, I // 2, dtype=torch.uint8, device=device)
     w2_s = torch.empty(El, D, I // 32, dtype=torch.uint8, device=device)
-    for e in range(e0, e0 + El):
+    if init == "random":
+        for t, hi in ((w13, 256), (w2, 256), (w13_s, 125), (w2_s, 125)):
+            t.copy_(torch.randint(0 if hi == 256 else 118, hi, t.shape, dtype=torch.uint8, device=device,
+                                  generator=g))
+    for e in range(e0, e0 + El) if init == "quant" else ():
         g.manual_seed(1000003 * (seed + 1) + e)
         a = (torch.randn(2 * I, D, device=device, generator=g) * 0.02).to(torch.bfloat16)
         wq, ws = ops.fp4_act_quant(a)
@@ -219,7 +226,7 @@ def run_gpu(args):
                                 device_id=dev)
     T = args.tokens
     Tg = T * world
-    layers = [make_layer(s, rank, world, max(Tg, 16), dev) for s in range(args.layers)]
+    layers = [make_layer(s, rank, world, max(Tg, 16), dev, args.init) for s in range(args.layers)]
     lib = L.load()
     hbm, peak_kind = peaks()
     torch.cuda.synchronize()
@@ -235,6 +242,9 @@ def run_gpu(args):
         ys = [torch.empty(Tloc, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
         idx = [torch.empty(Tloc * world, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+        for row in evs:  # torch creates the CUDA event on first record
+            for e in row:
+                e.record()
         Tgl = Tloc * world
         xg = [torch.empty(Tgl, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
         part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]

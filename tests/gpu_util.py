@@ -80,3 +80,30 @@ def near_tie_rows(x, layer, ids=None, eps=1e-6):
         return np.zeros(x.shape[0], bool)
     _, _, biased = O.gate(x, layer.gate_w, layer.gate_b, s.topk, s.score_func, s.route_scale)
     return O.topk_margin(biased, s.topk) < eps
+
+
+def assert_layer_close_envelope(y, y_exact, y_fp32, what=""):
+    """``assert_layer_close`` against the oracle, with the reference's own spread.
+
+    ``y_exact`` and ``y_fp32`` are the oracle evaluated with exact (fp64) and
+    fp32 (the reference's sgemm) matrix sums.  An element on which those two
+    disagree by more than the tolerance is not pinned down by the reference
+    itself (with non-power-of-two activation scales a 1-ulp change of one
+    intermediate value re-rounds a whole 128-block); such elements must lie
+    within twice that spread plus the tolerance.  All other elements, and the
+    MAE over all elements, get the plain tolerance.
+    """
+    y = np.asarray(y, np.float32)
+    y_exact = np.asarray(y_exact, np.float32)
+    y_fp32 = np.asarray(y_fp32, np.float32)
+    rms = float(np.sqrt(np.mean(y_exact.astype(np.float64) ** 2)))
+    floor = np.maximum(np.abs(y_exact), 0.01 * rms)
+    spread = np.abs(y_fp32 - y_exact)
+    ill = spread / floor > 1e-2
+    d = np.abs(y - y_exact)
+    assert np.isfinite(y).all(), f"{what}: non-finite output"
+    assert d.mean() <= 2e-3, f"{what}: MAE {d.mean():.3e} > 2e-3"
+    rel = d / floor
+    assert rel[~ill].max(initial=0.0) <= 1e-2, f"{what}: max rel err {rel[~ill].max():.3e} > 1e-2"
+    assert (d[ill] <= 2 * spread[ill] + 1e-2 * floor[ill]).all(), f"{what}: outside the reference's spread"
+    return int(ill.sum())

@@ -1,0 +1,120 @@
+"""Expert-parallel host logic on 2 CPU ranks (gloo).
+
+``wanferenz_b200.ep.ep_forward`` (all-gather tokens, local-expert partials,
+reduce-scatter, shared expert of the owned rows) is driven with a CPU stand-in
+layer whose partials come from the oracle's expert-range forward
+(architecture.py:749-756, 785-792).  The result must equal the single-process
+oracle up to the fp32 summation order of the partials.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import fixtures as F
+from oracle import moe_oracle as O
+
+SPEC = F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="sigmoid", route_scale=1.5, seed=51)
+
+
+class OracleShard:
+    """CPU stand-in with MoELayer's forward(partial=True) / finish(row0) contract."""
+
+    def __init__(self, syn, lo, hi):
+        self.syn, self.lo, self.hi = syn, lo, hi
+        self.shared_out = None
+
+    def forward(self, x, input_ids=None, partial=False):
+        xf = x.float().numpy()
+        p, _, _ = O.moe_forward(xf, self.syn.params(), None, expert_range=(self.lo, self.hi),
+                                return_partial=True)
+        self.shared_out = O.expert_fp8(xf, *self.syn.shared(), weights=None,
+                                       swiglu_limit=SPEC.swiglu_limit, ue8m0=SPEC.ue8m0)
+        return torch.from_numpy(p)
+
+    def finish(self, y_partial, row0=0):
+        T = y_partial.size(0)
+        y = y_partial.numpy() + self.shared_out[row0:row0 + T]
+        return torch.from_numpy(O.round_bf16(y.astype(np.float32))).to(torch.bfloat16)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, T, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from wanferenz_b200.ep import ep_forward, shard_range
+
+        syn = F.SyntheticLayer(SPEC)
+        x16, _ = syn.activations(T * world, draw=rank * 0 + 5)
+        x = torch.from_numpy(O.bf16_to_f32(x16)).to(torch.bfloat16)
+        mine = x[rank * T:(rank + 1) * T]
+        lo, hi = shard_range(SPEC.E, world, rank)
+        y = ep_forward(OracleShard(syn, lo, hi), mine)
+        q.put((rank, y.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_ep_forward_two_ranks_matches_single_process(T):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    syn = F.SyntheticLayer(SPEC)
+    x16, _ = syn.activations(T * world, draw=5)
+    y_ref, _, _ = O.moe_forward(O.bf16_to_f32(x16), syn.params(), None)
+    got = np.concatenate([out[0], out[1]])
+    d = np.abs(got - y_ref)
+    assert d.mean() <= 2e-3
+    assert (d / np.maximum(np.abs(y_ref), 0.01 * np.sqrt((y_ref ** 2).mean()))).max() <= 1e-2
+
+
+def _dead_worker(rank, world, port, q):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # this rank leaves between steps, with nothing in flight
+    try:
+        t = torch.zeros(4)
+        dist.all_reduce(t)
+        q.put("completed")
+    except Exception as e:  # the survivor must see an error, not hang
+        q.put(type(e).__name__)
+
+
+def test_lost_rank_surfaces_as_error_not_hang():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res != "completed"
