@@ -235,38 +235,38 @@ def run_gpu(args):
         if world > 1:
             dist.barrier()
 
-    def measure(Tloc, K, W, graph=True):
-        """K graph-captured steps; returns per-step times and per-kernel event times."""
+    def measure(Tloc, K, W):
+        """K graph-captured steps (headline time) + K eager steps with per-kernel events."""
         n = K + W
+        Tgl = Tloc * world
         xs = [torch.randn(Tloc, D, device=dev).to(torch.bfloat16) for _ in range(n)]
         ys = [torch.empty(Tloc, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
-        idx = [torch.empty(Tloc * world, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
+        idx = [torch.empty(Tgl, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
         for row in evs:  # torch creates the CUDA event on first record
             for e in row:
                 e.record()
-        Tgl = Tloc * world
         xg = [torch.empty(Tgl, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
         part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]
         mine = [torch.empty(Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
 
-        def one(i):
+        def one(i, timed=False):
             lay = layers[i % len(layers)]
             st = L.stream_ptr()
             ev = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in evs[i]])
-            if world == 1:
-                rc = lib.wf_moe_forward_timed(ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct),
-                                              L.ptr(xs[i]), 0, Tloc, L.ptr(ys[i]), 0, 0, L.ptr(idx[i]),
-                                              L.ptr(lay.workspace), lay.workspace.numel(), st, ev)
-                L.check(rc, "wf_moe_forward_timed")
-            else:
+            x_in, T_in = (xs[i], Tloc) if world == 1 else (xg[i], Tgl)
+            if world > 1:
                 dist.all_gather_into_tensor(xg[i], xs[i])
-                rc = lib.wf_moe_forward_timed(ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct),
-                                              L.ptr(xg[i]), 0, Tgl, 0, L.ptr(part[i]), 0, L.ptr(idx[i]),
-                                              L.ptr(lay.workspace), lay.workspace.numel(), st, ev)
-                L.check(rc, "wf_moe_forward_timed")
+            args_ = (ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(x_in), 0, T_in,
+                     L.ptr(ys[i]) if world == 1 else 0, 0 if world == 1 else L.ptr(part[i]), 0,
+                     L.ptr(idx[i]), L.ptr(lay.workspace), lay.workspace.numel(), st)
+            if timed:
+                L.check(lib.wf_moe_forward_timed(*args_, ev), "wf_moe_forward_timed")
+            else:
+                L.check(lib.wf_moe_forward(*args_), "wf_moe_forward")
+            if world > 1:
                 dist.reduce_scatter_tensor(mine[i], part[i])
-                # shared expert output of this rank's rows + bf16 cast (architecture.py:793-794)
+                # shared expert rows of this rank + bf16 cast (architecture.py:793-794)
                 L.check(lib.wf_moe_finish(ctypes.byref(lay.cfg), L.ptr(mine[i]), Tloc, rank * Tloc,
                                           L.ptr(ys[i]), L.ptr(lay.workspace), lay.workspace.numel(), st),
                         "wf_moe_finish")
@@ -275,11 +275,12 @@ def run_gpu(args):
             one(i)
         torch.cuda.synchronize()
         g = None
-        if graph and world == 1:
+        if world == 1:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 for i in range(W, n):
                     one(i)
+            g.replay()  # one untimed replay (graph upload)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -296,6 +297,15 @@ def run_gpu(args):
             torch.cuda.synchronize()
         barrier()
         total_ms = t0.elapsed_time(t1)
+        # per-kernel durations: eager steps queued behind ~2 ms of copies, so the
+        # host runs ahead of the GPU and no launch gap falls inside a kernel's events
+        big = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+        for _ in range(6):
+            big.add_(1)
+        for i in range(W, n):
+            one(i, timed=True)
+        torch.cuda.synchronize()
+        del big
         kern = {"k_moe_up": [], "k_moe_mid": [], "k_moe_down": []}
         for i in range(W, n):
             e = evs[i]
@@ -366,7 +376,7 @@ def run_gpu(args):
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / hbm, 4),
                      "traffic": None, "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
         "clocks": main["clocks"],
-        "gpu_launches": 3 * args.steps * (2 if world > 1 else 1) - (args.steps if world > 1 else 0),
+        "gpu_launches": 3 * args.steps if world == 1 else 4 * args.steps,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

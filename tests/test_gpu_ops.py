@@ -69,7 +69,8 @@ def test_fp4_gemm_golden():
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 12288, 4096), (16, 4096, 4096), (5, 1024, 4096),
-                                   (3, 512, 2048), (9, 2048, 1024)])
+                                   (3, 512, 2048), (9, 2048, 1024), (4, 4096, 16384), (16, 1024, 8192),
+                                   (8, 129280, 4096), (1, 32768, 1024)])
 @pytest.mark.parametrize("scale", ["e8m0", "f32"])
 def test_fp8_gemm_vs_oracle(M, N, K, scale):
     """BASELINE config 3 shapes with K <= 4096 (fp32 weight scales per 128x128)."""
@@ -90,6 +91,21 @@ def test_fp8_gemm_vs_oracle(M, N, K, scale):
     aq_o, as_o = O.act_quant(O.bf16_to_f32(a16), 128, ue)
     c_ref = O.fp8_gemm(aq_o, as_o, bq, bs)
     U.assert_layer_close(U.to_f32(c), c_ref, f"fp8 {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 4096, 8192), (12, 2048, 2048)])
+def test_fp4_gemm_vs_oracle(M, N, K):
+    """fp4_gemm (torch_ops.py:102-108), including split-K (K > 4096)."""
+    ops = _ops()
+    a16 = F.normal_bf16((211, M, N, K), (M, K), 1.0)
+    rng = F.rng(212, N, K)
+    wq = rng.integers(0, 256, size=(N, K // 2)).astype(np.uint8)
+    ws = rng.integers(116, 126, size=(N, K // 32)).astype(np.uint8)
+    aq, as_ = ops.act_quant(U.bf16_tensor(a16), 128, "ue8m0", torch.float8_e8m0fnu)
+    c = ops.fp4_gemm(aq, as_, U.u8_tensor(wq).view(torch.float4_e2m1fn_x2),
+                     U.u8_tensor(ws).view(torch.float8_e8m0fnu))
+    aq_o, as_o = O.act_quant(O.bf16_to_f32(a16), 128, True)
+    U.assert_layer_close(U.to_f32(c), O.fp4_gemm(aq_o, as_o, wq, ws), f"fp4 {M}x{N}x{K}")
 
 
 def test_grouped_fp4_gemm_vs_oracle():

@@ -105,12 +105,17 @@ struct DenseArgs {
     const void *b_s;              // scales
     __nv_bfloat16 *out;           // [M, N]
     int rows, stride;             // rows per item, smem row stride
+    int nkc, Kc;                  // K chunks (split-K) and chunk length
+    float *part;                  // [nkc, M, N] fp32 partials (nkc > 1)
+    unsigned *cnt;                // [M-groups * N/rows] arrival counters (nkc > 1)
     int *err;
 };
 
 struct Item {
-    int ep, bsrc, fmt, K, stride;
+    int ep, bsrc, fmt, K, stride;  // K: columns this item covers
     int nrun, rrows;
+    int gpitch, spitch;            // global bytes between consecutive weight / scale rows
+    int kb0, kc;                   // first 128-block of K this item covers, K chunk index
     const uint8_t *wsrc[2];
     const uint8_t *ssrc[2];
     int grow[2];
@@ -136,12 +141,14 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
     const int D = a.D, I = a.I;
     it.ssrc[0] = it.ssrc[1] = nullptr;
     it.grow[0] = it.grow[1] = 0;
-    it.rb = 0;
+    it.rb = 0; it.kb0 = 0; it.kc = 0;
     if (kid == KID_UP) {  // shared expert w1/w3 rows + SwiGLU
-        const int TG = cdiv(a.T, TPI);
-        const int hb = i / TG, tg = i % TG, nh = a.g.nhs13;
+        // token group outer, row block inner: a CTA's contiguous range keeps
+        // one token group (its B fragments stay in registers)
+        const int nh = a.g.nhs13, nhb = I / nh;
+        const int tg = i / nhb, hb = i % nhb;
         it.ep = EP_SSWIGLU; it.bsrc = BS_XTOK; it.fmt = FMT_FP8; it.K = D; it.stride = a.g.st_s13;
-        it.nrun = 2; it.rrows = nh;
+        it.nrun = 2; it.rrows = nh; it.gpitch = D; it.spitch = 0;
         it.grow[0] = hb * nh; it.grow[1] = I + hb * nh;
         it.wsrc[0] = a.sw13 + (size_t)it.grow[0] * D;
         it.wsrc[1] = a.sw13 + (size_t)it.grow[1] * D;
@@ -149,10 +156,10 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
         return it;
     }
     if (kid == KID_MID && i >= n_it2) {  // shared expert w2
-        const int j = i - n_it2, TG = cdiv(a.T, TPI);
-        const int rb = j / TG, tg = j % TG, nr = a.g.rs2;
+        const int j = i - n_it2, nr = a.g.rs2, nrb = D / nr;
+        const int tg = j / nrb, rb = j % nrb;
         it.ep = EP_SOUT; it.bsrc = BS_HS; it.fmt = FMT_FP8; it.K = I; it.stride = a.g.st_s2;
-        it.nrun = 1; it.rrows = nr;
+        it.nrun = 1; it.rrows = nr; it.gpitch = I; it.spitch = 0;
         it.grow[0] = rb * nr;
         it.wsrc[0] = a.sw2 + (size_t)it.grow[0] * I;
         it.wsrc[1] = it.wsrc[0];
@@ -164,8 +171,8 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
     const int ai = find_active(pref, n_act, i);
     const int local = i - __ldg(pref + ai);
     const int p0 = __ldg(a.act_off + ai), ta = __ldg(a.act_off + ai + 1) - p0;
-    const int TGa = cdiv(ta, TPI);
-    const int blk = local / TGa, tg = local % TGa;
+    const int nblk = (kid == KID_MID) ? I / a.g.nh13 : D / a.g.r2;
+    const int tg = local / nblk, blk = local % nblk;
     const int el = __ldg(a.act_expert + ai) - a.e0;
     it.a = ai; it.tok0 = p0 + tg * TPI; it.ntok = min(TPI, ta - tg * TPI);
     if (kid == KID_MID) {  // routed w1/w3 rows + SwiGLU
@@ -173,7 +180,7 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
         const uint8_t *wb = a.w13 + (size_t)el * (2 * I) * (D / 2);
         const uint8_t *sb = a.w13_s + (size_t)el * (2 * I) * (D / 32);
         it.ep = EP_RSWIGLU; it.bsrc = BS_XPAIR; it.fmt = FMT_FP4; it.K = D; it.stride = a.g.st_w13;
-        it.nrun = 2; it.rrows = nh;
+        it.nrun = 2; it.rrows = nh; it.gpitch = D / 2; it.spitch = D / 32;
         it.grow[0] = blk * nh; it.grow[1] = I + blk * nh;
         it.wsrc[0] = wb + (size_t)it.grow[0] * (D / 2);
         it.wsrc[1] = wb + (size_t)it.grow[1] * (D / 2);
@@ -185,7 +192,7 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
         const uint8_t *wb = a.w2 + (size_t)el * D * (I / 2);
         const uint8_t *sb = a.w2_s + (size_t)el * D * (I / 32);
         it.ep = EP_ROUT; it.bsrc = BS_H; it.fmt = FMT_FP4; it.K = I; it.stride = a.g.st_w2;
-        it.nrun = 1; it.rrows = nr;
+        it.nrun = 1; it.rrows = nr; it.gpitch = I / 2; it.spitch = I / 32;
         it.grow[0] = blk * nr;
         it.wsrc[0] = wb + (size_t)it.grow[0] * (I / 2);
         it.wsrc[1] = it.wsrc[0];
@@ -197,31 +204,36 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
 }
 
 __device__ Item decode_dense(const DenseArgs &d, int i) {
+    // order: K chunk, then token group (or group g), then row block fastest, so a
+    // CTA's contiguous item range shares one activation slice (B in registers)
     Item it;
     const int nrb = d.N / d.rows;
-    int rb, tok0, ntok, gsel = 0;
-    if (d.G > 0) {  // grouped: item = (g, rb), one token (row g of a)
-        gsel = i / nrb; rb = i % nrb; tok0 = gsel; ntok = 1;
-    } else {
-        const int TG = cdiv(d.M, TPI);
-        rb = i / TG; const int tg = i % TG;
-        tok0 = tg * TPI; ntok = min(TPI, d.M - tok0);
-    }
-    it.ep = EP_DENSE; it.bsrc = BS_PREQ; it.fmt = d.wfmt; it.K = d.K; it.stride = d.stride;
-    it.nrun = 1; it.rrows = d.rows; it.rb = rb;
+    const int ntg = d.G > 0 ? d.G : cdiv(d.M, TPI);
+    const int kc = i / (ntg * nrb), rem = i % (ntg * nrb);
+    const int tg = rem / nrb, rb = rem % nrb;
+    int tok0, ntok, gsel = 0;
+    if (d.G > 0) { gsel = tg; tok0 = tg; ntok = 1; }
+    else { tok0 = tg * TPI; ntok = min(TPI, d.M - tok0); }
+    it.ep = EP_DENSE; it.bsrc = BS_PREQ; it.fmt = d.wfmt; it.K = d.Kc; it.stride = d.stride;
+    it.nrun = 1; it.rrows = d.rows; it.rb = tg * nrb + rb; it.kc = kc;
+    it.kb0 = kc * (d.Kc / 128);
     it.grow[0] = rb * d.rows; it.grow[1] = 0;
     const size_t rowb = d.wfmt == FMT_FP4 ? (size_t)d.K / 2 : (size_t)d.K;
+    it.gpitch = (int)rowb;
     const uint8_t *wbase = d.b + (size_t)gsel * d.N * rowb;
-    it.wsrc[0] = wbase + (size_t)it.grow[0] * rowb;
+    const size_t koff = d.wfmt == FMT_FP4 ? (size_t)kc * d.Kc / 2 : (size_t)kc * d.Kc;
+    it.wsrc[0] = wbase + (size_t)it.grow[0] * rowb + koff;
     it.wsrc[1] = it.wsrc[0];
     if (d.wfmt == FMT_FP4) {
+        it.spitch = d.K / 32;
         const uint8_t *sbase = (const uint8_t *)d.b_s + (size_t)gsel * d.N * (d.K / 32);
-        it.ssrc[0] = sbase + (size_t)it.grow[0] * (d.K / 32);
+        it.ssrc[0] = sbase + (size_t)it.grow[0] * (d.K / 32) + (size_t)kc * d.Kc / 32;
     } else {
+        it.spitch = 0;
         it.ssrc[0] = nullptr;
     }
     it.ssrc[1] = it.ssrc[0];
-    it.row0 = it.grow[0]; it.a = gsel; it.tok0 = tok0; it.ntok = ntok;
+    it.row0 = it.grow[0]; it.a = gsel * 65536 + kc; it.tok0 = tok0; it.ntok = ntok;
     return it;
 }
 
@@ -270,11 +282,18 @@ __device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode)
         uint8_t *dst = sm.slot(s);
         for (int run = 0; run < it.nrun; ++run) {
             for (int r = 0; r < it.rrows; ++r)
-                bulk_g2s(dst + (run * it.rrows + r) * it.stride, it.wsrc[run] + (size_t)r * rowb,
-                         rowb, sm.full(s));
-            if (it.fmt == FMT_FP4)
-                bulk_g2s(dst + SLOT_W + run * it.rrows * ks, it.ssrc[run], it.rrows * ks,
-                         sm.full(s));
+                bulk_g2s(dst + (run * it.rrows + r) * it.stride,
+                         it.wsrc[run] + (size_t)r * it.gpitch, rowb, sm.full(s));
+            if (it.fmt == FMT_FP4) {
+                if ((uint32_t)it.spitch == ks) {  // the run's scale rows are contiguous
+                    bulk_g2s(dst + SLOT_W + run * it.rrows * ks, it.ssrc[run], it.rrows * ks,
+                             sm.full(s));
+                } else {  // split-K chunk: one copy per row (ks is a multiple of 16 here)
+                    for (int r = 0; r < it.rrows; ++r)
+                        bulk_g2s(dst + SLOT_W + (run * it.rrows + r) * ks,
+                                 it.ssrc[run] + (size_t)r * it.spitch, ks, sm.full(s));
+                }
+            }
         }
     }
     // drain: every armed phase must complete before the CTA may exit
@@ -399,7 +418,7 @@ template <typename FP8Scale>
 __device__ __forceinline__ float fp8_row_scale(const Item &it, int arow, int kb, FP8Scale f8s) {
     const int run = arow / it.rrows;
     const int grow = it.grow[run] + (arow - run * it.rrows);
-    return f8s(grow / 128, kb);
+    return f8s(grow / 128, it.kb0 + kb);
 }
 
 // One item's main loop for one consumer warp: acc[m][nt][c] over the warp's K segments.
@@ -1012,7 +1031,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ Dense
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
-    const int n = (d.N / d.rows) * (d.G > 0 ? d.G : cdiv(d.M, TPI));
+    const int n = d.nkc * (d.N / d.rows) * (d.G > 0 ? d.G : cdiv(d.M, TPI));
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_dense(d, i); };
@@ -1021,21 +1040,46 @@ __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ Dense
         return;
     }
     auto rowptr = [&](const Item &it, int j) -> const void * {
-        return d.a + (size_t)(it.tok0 + j) * d.K;
+        return d.a + (size_t)(it.tok0 + j) * d.K + (size_t)it.kc * d.Kc;
     };
     auto preq = [&](const Item &it, int j, int s) {
-        const size_t ix = (size_t)(it.tok0 + j) * (d.K / 128) + s;
+        const size_t ix = (size_t)(it.tok0 + j) * (d.K / 128) + it.kb0 + s;
         return d.a_f32 ? __ldg((const float *)d.a_s + ix) : e8m0_to_f32(__ldg((const uint8_t *)d.a_s + ix));
     };
     auto f8 = [&](int rblk, int kb) {
         const size_t ix = (size_t)rblk * (d.K / 128) + kb;
         return d.b_f32 ? __ldg((const float *)d.b_s + ix) : e8m0_to_f32(__ldg((const uint8_t *)d.b_s + ix));
     };
+    volatile int *flag = sm.flags() + 1;
     auto epi = [&](const Item &it, const float *red, int tid) {
         const int nr = it.rrows;
+        const int M = d.G > 0 ? d.G : d.M;
+        if (d.nkc == 1) {
+            for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
+                const int tok = idx / nr, r = idx % nr;
+                d.out[(size_t)(it.tok0 + tok) * d.N + it.row0 + r] = __float2bfloat16_rn(red_sum(red, r, tok));
+            }
+            return;
+        }
+        // split-K: fp32 partial per chunk; the last chunk to arrive sums them in chunk order
         for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
             const int tok = idx / nr, r = idx % nr;
-            d.out[(size_t)(it.tok0 + tok) * d.N + it.row0 + r] = __float2bfloat16_rn(red_sum(red, r, tok));
+            d.part[((size_t)it.kc * M + it.tok0 + tok) * d.N + it.row0 + r] = red_sum(red, r, tok);
+        }
+        __threadfence();
+        bar_sync(1, NCT);
+        if (tid == 0) *flag = (atomicAdd(d.cnt + it.rb, 1u) == (unsigned)d.nkc - 1);
+        bar_sync(1, NCT);
+        if (*flag) {
+            __threadfence();
+            for (int idx = tid; idx < nr * it.ntok; idx += NCT) {
+                const int tok = idx / nr, r = idx % nr;
+                float v = 0.f;
+                for (int c = 0; c < d.nkc; ++c)
+                    v += __ldcg(d.part + ((size_t)c * M + it.tok0 + tok) * d.N + it.row0 + r);
+                d.out[(size_t)(it.tok0 + tok) * d.N + it.row0 + r] = __float2bfloat16_rn(v);
+            }
+            if (tid == 0) d.cnt[it.rb] = 0u;
         }
     };
     consume(sm, i0, i1, 1, d.err, decode, rowptr, preq, f8, epi);
@@ -1429,19 +1473,52 @@ int wf_fp4_act_quant(const void *x, int64_t M, int64_t K, void *q, void *s, void
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "fp4_act_quant launch");
 }
 
-size_t wf_gemm_workspace_bytes(int64_t, int64_t, int64_t) { return 256; }
+static int gemm_chunks(int64_t K) { return (int)((K + wf::KMAX - 1) / wf::KMAX); }
+
+static int gemm_rows(int wfmt, int64_t N, int64_t K) {
+    const int nkc = gemm_chunks(K);
+    const int Kc = (int)(K / nkc);
+    const int fit = rows_fit(wfmt == wf::FMT_FP4 ? stride_fp4(Kc) : stride_fp8(Kc));
+    return (fit >= 32 && N % 32 == 0) ? 32 : (fit >= 16 && N % 16 == 0) ? 16 : 8;
+}
+
+struct GemmWs {
+    size_t cnt, part, total;
+};
+
+static GemmWs gemm_ws(int64_t M, int64_t N, int64_t K, int rows) {
+    GemmWs w{};
+    const int nkc = gemm_chunks(K);
+    w.cnt = 256;
+    if (nkc <= 1) { w.part = w.total = 256; return w; }
+    // counters per (token group or slot, row block): M * N/rows bounds both cases
+    const size_t groups = (size_t)M * (N / rows);
+    w.part = w.cnt + align256(groups * 4);
+    w.total = w.part + align256((size_t)nkc * M * N * 4);
+    return w;
+}
+
+size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % 8) return 0;
+    // sized for the finer of the FP8 / FP4 row blockings
+    const int rows = std::min(gemm_rows(wf::FMT_FP8, N, K), gemm_rows(wf::FMT_FP4, N, K));
+    return gemm_ws(M, N, K, rows).total;
+}
 
 static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const void *b,
                  const void *b_s, int b_kind, int64_t M, int64_t N, int64_t K, int64_t G,
                  void *out, void *ws, size_t ws_bytes, cudaStream_t st) {
-    if (!a || !a_s || !b || !b_s || !out) return fail(WF_E_ARG, "null pointer");
-    if (!ws || ws_bytes < 16) return fail(WF_E_ARG, "workspace too small");
-    if (M <= 0 || N <= 0 || K <= 0 || K % 128 || K > wf::KMAX || N % 8)
-        return fail(WF_E_SHAPE, "need K a multiple of 128 (<= 4096) and N a multiple of 8");
+    if (!a || !a_s || !b || !b_s || !out || !ws) return fail(WF_E_ARG, "null pointer");
+    const int nkc = K > 0 ? gemm_chunks(K) : 0;
+    if (M <= 0 || N <= 0 || K <= 0 || N % 8 || K % (128 * nkc))
+        return fail(WF_E_SHAPE, "need N a multiple of 8 and K a multiple of 128 per 4096-wide chunk");
     if ((a_kind != WF_SCALE_F32 && a_kind != WF_SCALE_E8M0) ||
         (b_kind != WF_SCALE_F32 && b_kind != WF_SCALE_E8M0))
         return fail(WF_E_DTYPE, "bad scale kind");
-    if (M > (1 << 30) || N > (1 << 30) || G > (1 << 20)) return fail(WF_E_SHAPE, "too large");
+    if (M > (1 << 24) || N > (1 << 26) || G > (1 << 16) || K > (1 << 20)) return fail(WF_E_SHAPE, "too large");
+    const int rows = gemm_rows(wfmt, N, K);
+    const GemmWs L = gemm_ws(G > 0 ? G : M, N, K, rows);
+    if (ws_bytes < L.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
     int rc = ensure_attrs();
     if (rc) return rc;
     wf::DenseArgs d;
@@ -1449,10 +1526,13 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     d.wfmt = wfmt; d.a_f32 = a_kind == WF_SCALE_F32; d.b_f32 = b_kind == WF_SCALE_F32;
     d.a = (const uint8_t *)a; d.a_s = a_s; d.b = (const uint8_t *)b; d.b_s = b_s;
     d.out = (__nv_bfloat16 *)out; d.err = (int *)ws;
-    d.stride = wfmt == wf::FMT_FP4 ? stride_fp4((int)K) : stride_fp8((int)K);
-    const int fit = rows_fit(d.stride);
-    d.rows = (fit >= 32 && N % 32 == 0) ? 32 : (fit >= 16 && N % 16 == 0) ? 16 : 8;
+    d.nkc = nkc; d.Kc = (int)(K / nkc);
+    d.stride = wfmt == wf::FMT_FP4 ? stride_fp4(d.Kc) : stride_fp8(d.Kc);
+    d.rows = rows;
+    d.cnt = (unsigned *)((uint8_t *)ws + L.cnt);
+    d.part = (float *)((uint8_t *)ws + L.part);
     const int G_ = sm_count();
+    if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
     wf::k_dense<<<G_, wf::NTHR, wf::SMEM_BYTES, st>>>(d);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "gemm launch");

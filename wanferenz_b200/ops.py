@@ -41,11 +41,16 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.uint8)
 
 
-def _gemm_ws(device) -> torch.Tensor:
+def _gemm_ws(device, m, n, k) -> torch.Tensor:
+    """Per-device workspace, grown to the largest (M, N, K) seen; zero-filled when allocated
+    (its split-K counters return to zero after every call)."""
+    need = L.load().wf_gemm_workspace_bytes(m, n, k)
+    if need == 0:
+        raise ValueError(f"unsupported GEMM shape M={m} N={n} K={k}")
     key = (device.type, device.index)
     ws = _GEMM_WS.get(key)
-    if ws is None:
-        ws = _GEMM_WS[key] = torch.zeros(256, dtype=torch.uint8, device=device)
+    if ws is None or ws.numel() < need:
+        ws = _GEMM_WS[key] = torch.zeros(need, dtype=torch.uint8, device=device)
     return ws
 
 
@@ -105,7 +110,7 @@ def fp8_gemm(a, a_s, b, b_s, scale_dtype=torch.float32):
     k, n = a.size(-1), b.size(0)
     m = a.numel() // k
     c = _out(a, n)
-    ws = _gemm_ws(a.device)
+    ws = _gemm_ws(a.device, m, n, k)
     L.check(lib.wf_fp8_gemm(L.ptr(_u8(a)), L.ptr(a_s.contiguous()), _kind(a_s), L.ptr(_u8(b)),
                             L.ptr(b_s.contiguous()), _kind(b_s), m, n, k, L.ptr(c), L.ptr(ws),
                             ws.numel(), L.stream_ptr()), "wf_fp8_gemm")
@@ -119,7 +124,7 @@ def fp4_gemm(a, a_s, b, b_s, scale_dtype=torch.float32):
     k, n = a.size(-1), b.size(0)
     m = a.numel() // k
     c = _out(a, n)
-    ws = _gemm_ws(a.device)
+    ws = _gemm_ws(a.device, m, n, k)
     L.check(lib.wf_fp4_gemm(L.ptr(_u8(a)), L.ptr(a_s.contiguous()), _kind(a_s), L.ptr(_u8(b)),
                             L.ptr(_u8(b_s)), m, n, k, L.ptr(c), L.ptr(ws), ws.numel(),
                             L.stream_ptr()), "wf_fp4_gemm")
@@ -133,7 +138,7 @@ def grouped_fp4_gemm(a, a_s, w, w_s, scale_dtype=torch.float32):
     g, k = a.shape
     n = w.size(1)
     c = torch.empty(g, n, dtype=torch.bfloat16, device=a.device)
-    ws = _gemm_ws(a.device)
+    ws = _gemm_ws(a.device, g, n, k)
     L.check(lib.wf_grouped_fp4_gemm(L.ptr(_u8(a)), L.ptr(a_s.contiguous()), _kind(a_s),
                                     L.ptr(_u8(w)), L.ptr(_u8(w_s)), g, n, k, L.ptr(c), L.ptr(ws),
                                     ws.numel(), L.stream_ptr()), "wf_grouped_fp4_gemm")
