@@ -300,7 +300,7 @@ def run_gpu(args):
         # per-kernel durations: eager steps queued behind ~2 ms of copies, so the
         # host runs ahead of the GPU and no launch gap falls inside a kernel's events
         big = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
-        for _ in range(6):
+        for _ in range(10):
             big.add_(1)
         for i in range(W, n):
             one(i, timed=True)

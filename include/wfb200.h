@@ -116,9 +116,9 @@ int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void
 
 /* wf_moe_forward with four caller-created cudaEvent_t recorded on `stream`
  * before the first and after each of the three kernels (measurement hook:
- * per-kernel durations without a profiler).  The records are "external", so
- * they also become event nodes when the stream is being captured into a CUDA
- * graph.  No counterpart in the reference. */
+ * per-kernel durations without a profiler; the kernels then launch without
+ * programmatic overlap, so each event pair brackets one kernel).  Not for use
+ * inside stream capture.  No counterpart in the reference. */
 int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
                          const int64_t *input_ids, int32_t T, void *y, float *y_partial,
                          float *out_weights, int64_t *out_indices, void *workspace,

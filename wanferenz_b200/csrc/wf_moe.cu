@@ -896,6 +896,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
+    pdl_wait();
+    pdl_launch_dependents();
     const int n = a.route_only ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
     int i0, i1;
     item_range(n, i0, i1);
@@ -942,6 +944,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
+    pdl_wait();
+    pdl_launch_dependents();
     const int n_act = a.hdr[H_NACT], n_it2 = a.hdr[H_IT2];
     const int n = n_it2 + (a.D / a.g.rs2) * cdiv(a.T, TPI);
     int i0, i1;
@@ -983,6 +987,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ Mo
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
+    pdl_wait();
+    pdl_launch_dependents();
     const int n_act = a.hdr[H_NACT], n = a.hdr[H_IT3], tgt = a.hdr[H_TGT];
     if (n_act == 0) {  // no local expert has tokens: y = shared part only
         if ((threadIdx.x >> 5) == NCW) return;
@@ -1364,16 +1370,35 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
     const int G = sm_count();
     if (G <= 0) return fail(WF_E_CUDA, "no CUDA device");
     a.route_only = route_only;
-    if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[0], st, cudaEventRecordExternal);
-    wf::k_moe_up<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
-    if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[1], st, cudaEventRecordExternal);
+    // Programmatic dependent launch: a kernel may begin launching while the one
+    // before it drains; each kernel waits (griddepcontrol.wait) before reading
+    // anything an earlier kernel wrote.  Event records break the overlap on
+    // purpose, so the timed variant launches without it.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ev ? 0 : 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(G);
+    lc.blockDim = dim3(wf::NTHR);
+    lc.dynamicSmemBytes = wf::SMEM_BYTES;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t e = cudaSuccess;
+    auto rec = [&](int i) {
+        if (ev && e == cudaSuccess)
+            e = cudaEventRecordWithFlags((cudaEvent_t)ev[i], st, cudaEventRecordDefault);
+    };
+    rec(0);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_up, a);
+    rec(1);
     if (!route_only) {
-        wf::k_moe_mid<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
-        if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[2], st, cudaEventRecordExternal);
-        wf::k_moe_down<<<G, wf::NTHR, wf::SMEM_BYTES, st>>>(a);
-        if (ev) cudaEventRecordWithFlags((cudaEvent_t)ev[3], st, cudaEventRecordExternal);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_mid, a);
+        rec(2);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_down, a);
+        rec(3);
     }
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "MoE kernel launch");
     return WF_OK;
 }

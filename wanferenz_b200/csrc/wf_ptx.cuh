@@ -78,6 +78,16 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// ---- programmatic dependent launch --------------------------------------
+// Lets the next kernel on the stream start launching (its CTAs run their
+// prologue) while this one drains.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Blocks until the previous kernel on the stream has completed and its memory
+// writes are visible; returns at once when launched without the PDL attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- named barrier among the consumer warps -----------------------------
 __device__ __forceinline__ void bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
