@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--sweep", default="1,4,16", help="extra token counts measured at N=1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--routing", default="uniform", choices=("uniform", "zipf"),
+                    help="zipf: BASELINE config 4 popularity, gate bias += beta*log(rank^-1.2)")
+    ap.add_argument("--zipf-beta", type=float, default=0.06)
     ap.add_argument("--init", default="quant", choices=("quant", "random"),
                     help="quant: N(0,0.02) weights through the FP4 quantizer; random: random FP4 bytes "
                          "with typical scales (fewer launches, for profiler captures)")
@@ -144,7 +147,7 @@ def fp8_block_quant_torch(w):
     return q.reshape(n, k).view(torch.uint8), scale.to(torch.float8_e8m0fnu).view(torch.uint8)
 
 
-def make_layer(seed, rank, world, max_tokens, device, init="quant"):
+def make_layer(seed, rank, world, max_tokens, device, init="quant", zipf_beta=0.0):
     import torch
 
     from wanferenz_b200 import ops
@@ -156,6 +159,12 @@ def make_layer(seed, rank, world, max_tokens, device, init="quant"):
     g.manual_seed(1000 + seed)  # router + shared: identical on every rank
     gate_w = (torch.randn(E, D, device=device, generator=g) * 0.02).to(torch.bfloat16)
     gate_b = torch.randn(E, device=device, generator=g) * 0.01
+    if zipf_beta > 0:
+        # Zipf(s=1.2) expert popularity over a seeded permutation
+        perm = torch.randperm(E, device=device, generator=g)
+        rank_of = torch.empty(E, device=device)
+        rank_of[perm] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
+        gate_b = gate_b + zipf_beta * torch.log(rank_of.pow(-1.2))
     sh = [(torch.randn(*shp, device=device, generator=g) * 0.02).to(torch.bfloat16)
           for shp in ((I, D), (I, D), (D, I))]
     q = [fp8_block_quant_torch(t) for t in sh]
@@ -226,7 +235,8 @@ def run_gpu(args):
                                 device_id=dev)
     T = args.tokens
     Tg = T * world
-    layers = [make_layer(s, rank, world, max(Tg, 16), dev, args.init) for s in range(args.layers)]
+    zb = args.zipf_beta if args.routing == "zipf" else 0.0
+    layers = [make_layer(s, rank, world, max(Tg, 16), dev, args.init, zb) for s in range(args.layers)]
     lib = L.load()
     hbm, peak_kind = peaks()
     torch.cuda.synchronize()
@@ -328,7 +338,12 @@ def run_gpu(args):
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
         layer_bytes = mean["k_moe_up"] + mean["k_moe_mid"] + mean["k_moe_down"]
-        return dict(ms=ms, total_ms=total_ms, kms=kms, bytes=mean, layer_bytes=layer_bytes, clocks=clk)
+        hist = [np.bincount(r.ravel(), minlength=E) for r in routing]
+        tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
+               "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
+               "max_tokens_per_expert": float(np.mean([h.max() for h in hist]))}
+        return dict(ms=ms, total_ms=total_ms, kms=kms, bytes=mean, layer_bytes=layer_bytes, clocks=clk,
+                    tpe=tpe)
 
     main = stats(T, args.steps, args.warmup)
     sweep = {}
@@ -360,7 +375,11 @@ def run_gpu(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32",
         "data": "synthetic (seeded N(0,0.02) weights quantized like the reference fixtures; N(0,1) bf16 tokens)",
         "config": {
-            "workload": f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing",
+            "workload": (f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing"
+                         if args.routing == "uniform" else
+                         f"BASELINE config 4: config-2 layer, {T} tokens per GPU, Zipf(1.2) routing "
+                         f"(gate bias beta={args.zipf_beta})"),
+            "routing": args.routing,
             "tokens_per_gpu": T, "global_tokens": T * world, "hidden": D, "experts": E, "inter": I,
             "topk": K_TOP, "layers_cycled": args.layers, "parallelism": f"ep{world}" if world > 1 else "single",
             "l2": f"{args.layers} distinct layers cycled (per-step weights cold in L2), no flush",
@@ -370,6 +389,7 @@ def run_gpu(args):
             "layer_GBps": round(main["layer_bytes"] / (main["ms"] * 1e-3) / 1e9, 1),
             "kernel_us": {k: round(v * 1e3, 2) for k, v in kms.items()},
             "experts_touched_per_rank": round(main["bytes"]["experts"], 1),
+            "tokens_per_expert": main["tpe"],
             "sweep": sweep,
         },
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,

@@ -176,10 +176,9 @@ int wf_grouped_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, co
 /* Workspace bytes for the dense GEMM entry points above. */
 size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
-/* Load-time check that every FP4 weight scale byte lies in [104, 140]
- * (2^-23 .. 2^13), the range in which the kernels' f16 prescale of E2M1
- * values is exact.  Synchronizes the stream.  Returns 1 (in range), 0 (not)
- * or a negative WF_E_* code. */
+/* Load-time check that no FP4 weight scale byte is 0 or 255 (2^-127, the
+ * subnormal the kernels do not decode, or NaN).  Synchronizes the stream.
+ * Returns 1 (in range), 0 (not) or a negative WF_E_* code. */
 int wf_fp4_scales_in_range(const uint8_t *scales, int64_t n, void *stream);
 
 #ifdef __cplusplus

@@ -12,13 +12,14 @@
 //             + per-row-block ascending-expert combine          -> y
 //
 // Each launch is a static, balanced split of "items" over the CTAs.  An item
-// is up to 32 weight rows (<= 34 KB) times up to 8 tokens.  Inside a CTA one
-// producer warp streams each item's rows into a 6-slot shared-memory ring with
+// is up to 32 weight rows (<= 34 KB) times up to 16 tokens.  Inside a CTA one
+// producer warp streams each item's rows into a 5-slot shared-memory ring with
 // bulk TMA copies (cp.async.bulk, completion on an mbarrier); eight consumer
-// warps split K, dequantize in registers (E2M1 -> f16 with the per-32 UE8M0
-// scale folded in, exact; E4M3 -> f16, exact), multiply on the tensor cores
-// (mma.m16n8k16, f32 accumulate), apply the per-128 activation scale in f32,
-// and reduce across warps in a fixed order through shared memory.
+// warps split K, dequantize FP4 in registers with integer ops (E2M1 -> E4M3
+// of value x 2^-6, exact; FP8 weights need no conversion), multiply on the
+// tensor cores (mma.m16n8k32 E4M3 x E4M3 -> f32), apply the per-32 weight and
+// per-128 activation scales in f32, and reduce across warps in a fixed order
+// through shared memory.
 // Activations are quantized to E4M3 (act_quant, torch_ops.py:33-49) by the
 // consumer warps themselves when they load a token's K-slice.
 
@@ -37,12 +38,12 @@ namespace wf {
 constexpr int NCW = 8;                 // consumer warps
 constexpr int NTHR = (NCW + 1) * 32;   // + 1 producer warp
 constexpr int NCT = NCW * 32;          // consumer threads
-constexpr int NSLOT = 6;               // ring slots
+constexpr int NSLOT = 5;               // ring slots
 constexpr int SLOT_W = 34816;          // weight bytes per slot (padded rows)
 constexpr int SLOT_S = 2048;           // FP4 scale bytes per slot
 constexpr int SLOT_BYTES = SLOT_W + SLOT_S;
 constexpr int MAXR = 32;               // weight rows per item
-constexpr int NTM = 1;                 // n-tiles (8 tokens each) per item
+constexpr int NTM = 2;                 // n-tiles (8 tokens each) per item
 constexpr int TPI = 8 * NTM;           // tokens per item
 constexpr int SPW = 4;                 // max 128-wide K segments per warp
 constexpr int KMAX = NCW * SPW * 128;  // longest K one item covers (4096)
@@ -51,10 +52,15 @@ constexpr int OFF_RED = NSLOT * SLOT_BYTES;
 constexpr int OFF_BAR = OFF_RED + RED_BYTES;
 constexpr int OFF_MISC = OFF_BAR + 2 * NSLOT * 8 + 64;
 constexpr int MISC_BYTES = 2048;  // router partial sums (fp64) / top-k expert counts
-constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES;
 constexpr int MAX_E = 512;
 constexpr int MAX_K = 8;
 constexpr int MAX_T = 256;
+constexpr int MAX_PAIRS = MAX_T * MAX_K;
+// routing tables copied to shared memory at kernel start (K2, K3)
+constexpr int OFF_ROUTE = OFF_MISC + MISC_BYTES;
+constexpr int ROUTE_BYTES = 3 * (MAX_E + 1) * 4 + MAX_PAIRS * 2 + MAX_PAIRS * 4;
+constexpr int SMEM_BYTES = OFF_ROUTE + ROUTE_BYTES;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 enum { EP_RSWIGLU = 1, EP_SSWIGLU = 2, EP_SOUT = 3, EP_ROUT = 4, EP_DENSE = 5 };
 enum { BS_XPAIR = 1, BS_XTOK = 2, BS_H = 3, BS_HS = 4, BS_PREQ = 5 };
@@ -127,16 +133,9 @@ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 // ---------------------------------------------------------------------------
 // item decoding (identical in producer and consumers)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int find_active(const int *prefix, int n_act, int i) {
-    int lo = 0, hi = n_act - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (__ldg(prefix + mid) <= i) lo = mid; else hi = mid - 1;
-    }
-    return lo;
-}
-
-__device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it2) {
+__device__ __forceinline__ Item decode_moe(int kid, const MoeArgs &a, int i, int ai, int n_it2,
+                                           const int *act_expert, const int *act_off,
+                                           const int *act_it) {
     Item it;
     const int D = a.D, I = a.I;
     it.ssrc[0] = it.ssrc[1] = nullptr;
@@ -166,14 +165,12 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
         it.row0 = rb * nr; it.a = 0; it.tok0 = tg * TPI; it.ntok = min(TPI, a.T - tg * TPI);
         return it;
     }
-    // routed items
-    const int *pref = (kid == KID_MID) ? a.act_it2 : a.act_it3;
-    const int ai = find_active(pref, n_act, i);
-    const int local = i - __ldg(pref + ai);
-    const int p0 = __ldg(a.act_off + ai), ta = __ldg(a.act_off + ai + 1) - p0;
+    // routed items (tables in shared memory)
+    const int local = i - act_it[ai];
+    const int p0 = act_off[ai], ta = act_off[ai + 1] - p0;
     const int nblk = (kid == KID_MID) ? I / a.g.nh13 : D / a.g.r2;
     const int tg = local / nblk, blk = local % nblk;
-    const int el = __ldg(a.act_expert + ai) - a.e0;
+    const int el = act_expert[ai] - a.e0;
     it.a = ai; it.tok0 = p0 + tg * TPI; it.ntok = min(TPI, ta - tg * TPI);
     if (kid == KID_MID) {  // routed w1/w3 rows + SwiGLU
         const int nh = a.g.nh13;
@@ -203,7 +200,7 @@ __device__ Item decode_moe(int kid, const MoeArgs &a, int i, int n_act, int n_it
     return it;
 }
 
-__device__ Item decode_dense(const DenseArgs &d, int i) {
+__device__ __forceinline__ Item decode_dense(const DenseArgs &d, int i) {
     // order: K chunk, then token group (or group g), then row block fastest, so a
     // CTA's contiguous item range shares one activation slice (B in registers)
     Item it;
@@ -254,6 +251,60 @@ struct Smem {
     __device__ double *misc() const { return reinterpret_cast<double *>(base + OFF_MISC); }
 };
 
+// Routing tables of the current forward, in shared memory.
+struct RouteSm {
+    int *act_expert, *act_off, *act_it;
+    int16_t *pair_tok;
+    float *pair_w;
+};
+
+__device__ __forceinline__ RouteSm route_sm(const Smem &sm) {
+    RouteSm r;
+    int *b = reinterpret_cast<int *>(sm.base + OFF_ROUTE);
+    r.act_expert = b;
+    r.act_off = b + (MAX_E + 1);
+    r.act_it = b + 2 * (MAX_E + 1);
+    r.pair_tok = reinterpret_cast<int16_t *>(b + 3 * (MAX_E + 1));
+    r.pair_w = reinterpret_cast<float *>(r.pair_tok + MAX_PAIRS);
+    return r;
+}
+
+// All 288 threads: copy the tables written by the router CTA (K1) into shared memory.
+__device__ __forceinline__ void load_route(const Smem &sm, const int *act_expert, const int *act_off,
+                                           const int *act_it, const int *pair_tok, const float *pair_w,
+                                           int n_act, int n_pairs) {
+    const RouteSm r = route_sm(sm);
+    for (int i = threadIdx.x; i <= n_act; i += blockDim.x) {
+        r.act_off[i] = act_off[i];
+        r.act_it[i] = act_it[i];
+        if (i < n_act) r.act_expert[i] = act_expert[i];
+    }
+    for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) {
+        r.pair_tok[i] = (int16_t)pair_tok[i];
+        r.pair_w[i] = pair_w[i];
+    }
+    __syncthreads();
+}
+
+// Walks a CTA's contiguous item range; `ai` tracks the active expert of item `i`.
+struct Cursor {
+    int i, ai;
+};
+
+__device__ __forceinline__ Cursor cursor_at(const RouteSm &r, int n_act, int i) {
+    int lo = 0, hi = n_act - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (r.act_it[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    return Cursor{i, lo};
+}
+
+__device__ __forceinline__ void cursor_next(const RouteSm &r, int n_act, Cursor &c) {
+    ++c.i;
+    while (c.ai + 1 < n_act && c.i >= r.act_it[c.ai + 1]) ++c.ai;
+}
+
 __device__ __forceinline__ void item_range(int n, int &i0, int &i1) {
     i0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
     i1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
@@ -280,18 +331,21 @@ __device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode)
         uint32_t bytes = na * rowb + (it.fmt == FMT_FP4 ? na * ks : 0);
         mbar_arrive_expect_tx(sm.full(s), bytes);
         uint8_t *dst = sm.slot(s);
-        for (int run = 0; run < it.nrun; ++run) {
+#pragma unroll
+        for (int run = 0; run < 2; ++run) {
+            if (run >= it.nrun) break;
+            const uint8_t *wsrc = run ? it.wsrc[1] : it.wsrc[0];
+            const uint8_t *ssrc = run ? it.ssrc[1] : it.ssrc[0];
             for (int r = 0; r < it.rrows; ++r)
-                bulk_g2s(dst + (run * it.rrows + r) * it.stride,
-                         it.wsrc[run] + (size_t)r * it.gpitch, rowb, sm.full(s));
+                bulk_g2s(dst + (run * it.rrows + r) * it.stride, wsrc + (size_t)r * it.gpitch, rowb,
+                         sm.full(s));
             if (it.fmt == FMT_FP4) {
                 if ((uint32_t)it.spitch == ks) {  // the run's scale rows are contiguous
-                    bulk_g2s(dst + SLOT_W + run * it.rrows * ks, it.ssrc[run], it.rrows * ks,
-                             sm.full(s));
+                    bulk_g2s(dst + SLOT_W + run * it.rrows * ks, ssrc, it.rrows * ks, sm.full(s));
                 } else {  // split-K chunk: one copy per row (ks is a multiple of 16 here)
                     for (int r = 0; r < it.rrows; ++r)
                         bulk_g2s(dst + SLOT_W + (run * it.rrows + r) * ks,
-                                 it.ssrc[run] + (size_t)r * it.spitch, ks, sm.full(s));
+                                 ssrc + (size_t)r * it.spitch, ks, sm.full(s));
                 }
             }
         }
@@ -308,8 +362,10 @@ __device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode)
 // consumers
 // ---------------------------------------------------------------------------
 struct BRegs {
-    uint32_t b[NTM][SPW][16];  // token slot g's K-slice as f16x2 E4M3 codes
-    float sx[NTM][SPW][2];     // activation scales of the C-fragment tokens
+    // token slot g's K-slice as packed E4M3 codes: per 128-wide segment, per
+    // 32-block j, the two m16n8k32 B registers {b0, b1} (see arrange_codes)
+    uint32_t b[NTM][SPW][8];
+    float sx[NTM][SPW][2];  // activation scales of the C-fragment tokens (x 2^6 for FP4 items)
 };
 
 __device__ __forceinline__ float round_scale_e8(float amax, int ue8m0) {
@@ -320,27 +376,38 @@ __device__ __forceinline__ float round_scale_e8(float amax, int ue8m0) {
     return __uint_as_float(((b >> 23) + 1) << 23);
 }
 
-// Quantize 32 bf16 values (act_quant semantics) into 16 f16x2 E4M3 codes;
-// the 4 lanes of a quad share one 128-block.  Returns the block scale.
-__device__ __forceinline__ float quant32(const __nv_bfloat16 *src, bool valid, int ue8m0,
-                                         uint32_t (&out)[16]) {
-    uint32_t w[16];
-    if (valid) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint4 u = ldg128(src + c * 8);
-            w[4 * c] = u.x; w[4 * c + 1] = u.y; w[4 * c + 2] = u.z; w[4 * c + 3] = u.w;
-        }
+// 8 E4M3 codes (lo = elements 0-3, hi = 4-7) -> the thread's two B registers.
+// FP4 items pair the MMA k-slots with even / odd elements (the even-odd split
+// of fp4_to_e4m3); FP8 items with the two contiguous halves.
+__device__ __forceinline__ void arrange_codes(uint32_t lo, uint32_t hi, bool interleave,
+                                              uint32_t &b0, uint32_t &b1) {
+    if (interleave) {
+        b0 = __byte_perm(lo, hi, 0x6420);  // elements 0, 2, 4, 6
+        b1 = __byte_perm(lo, hi, 0x7531);  // elements 1, 3, 5, 7
     } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) w[e] = 0u;
+        b0 = lo;
+        b1 = hi;
     }
-    // |bf16| max on the bit patterns: clearing the sign bits leaves an order-preserving integer
-    uint32_t amax_bits = 0;
+}
+
+// act_quant (torch_ops.py:33-49) of one token's 128-block, held as 4 chunks of
+// 8 bf16 per lane (chunk j = elements 32j + 8*tig .. +7); the quad's 4 lanes
+// share the block amax.  Writes the 8 B registers; returns the block scale.
+__device__ __forceinline__ float quant_seg(const __nv_bfloat16 *seg, int tig, bool valid, int ue8m0,
+                                           bool interleave, uint32_t (&out)[8]) {
+    uint4 w[4];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        amax_bits = max(amax_bits, w[e] & 0x7fffu);
-        amax_bits = max(amax_bits, (w[e] >> 16) & 0x7fffu);
+    for (int j = 0; j < 4; ++j)
+        w[j] = valid ? ldg128(seg + 32 * j + 8 * tig) : make_uint4(0, 0, 0, 0);
+    uint32_t amax_bits = 0;  // |bf16| max on bit patterns (sign cleared: order-preserving)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t v[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            amax_bits = max(amax_bits, v[e] & 0x7fffu);
+            amax_bits = max(amax_bits, (v[e] >> 16) & 0x7fffu);
+        }
     }
     float amax = bf16_bits_to_f32(amax_bits);
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -348,35 +415,43 @@ __device__ __forceinline__ float quant32(const __nv_bfloat16 *src, bool valid, i
     const float s = round_scale_e8(fmaxf(amax, 1e-4f), ue8m0);
     const float inv = 1.0f / s;  // exact when s is a power of two
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        float lo = bf16_bits_to_f32(w[e] & 0xffffu), hi = bf16_bits_to_f32(w[e] >> 16);
-        if (ue8m0) { lo *= inv; hi *= inv; }
-        else { lo = __fdiv_rn(lo, s); hi = __fdiv_rn(hi, s); }
-        lo = fminf(fmaxf(lo, -448.f), 448.f);
-        hi = fminf(fmaxf(hi, -448.f), 448.f);
-        out[e] = e4m3x2_to_f16x2(f32x2_to_e4m3x2(lo, hi));
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t v[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+        uint32_t q[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float lo = bf16_bits_to_f32(v[e] & 0xffffu), hi = bf16_bits_to_f32(v[e] >> 16);
+            if (ue8m0) { lo *= inv; hi *= inv; }
+            else { lo = __fdiv_rn(lo, s); hi = __fdiv_rn(hi, s); }
+            lo = fminf(fmaxf(lo, -448.f), 448.f);
+            hi = fminf(fmaxf(hi, -448.f), 448.f);
+            q[e] = f32x2_to_e4m3x2(lo, hi);  // 16 bits: element 2e low, 2e+1 high
+        }
+        const uint32_t lo4 = q[0] | (q[1] << 16), hi4 = q[2] | (q[3] << 16);
+        arrange_codes(lo4, hi4, interleave, out[2 * j], out[2 * j + 1]);
     }
     return valid ? s : 0.f;
 }
 
-// Pre-quantized E4M3 codes (32 bytes) -> 16 f16x2
-__device__ __forceinline__ void codes32(const uint8_t *src, bool valid, uint32_t (&out)[16]) {
-    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
-    if (valid) { u0 = ldg128(src); u1 = ldg128(src + 16); }
-    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+// Pre-quantized E4M3 codes of one 128-block (4 chunks of 8 bytes per lane).
+__device__ __forceinline__ void codes_seg(const uint8_t *seg, int tig, bool valid, bool interleave,
+                                          uint32_t (&out)[8]) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        out[2 * e] = e4m3x2_to_f16x2((uint16_t)(w[e] & 0xffffu));
-        out[2 * e + 1] = e4m3x2_to_f16x2((uint16_t)(w[e] >> 16));
+    for (int j = 0; j < 4; ++j) {
+        uint2 u = make_uint2(0, 0);
+        if (valid) u = __ldg(reinterpret_cast<const uint2 *>(seg + 32 * j + 8 * tig));
+        arrange_codes(u.x, u.y, interleave, out[2 * j], out[2 * j + 1]);
     }
 }
 
 template <typename RowPtr, typename PreqScale>
-__device__ void load_b(const Item &it, int warp, int lane, int ue8m0, BRegs &B, RowPtr rowptr,
-                       PreqScale preq_scale) {
+__device__ __forceinline__ void load_b(const Item &it, int warp, int lane, int ue8m0, BRegs &B,
+                                       RowPtr rowptr, PreqScale preq_scale) {
     const int g = lane >> 2, tig = lane & 3;
     const int nseg = it.K / 128, spw = cdiv(nseg, NCW), s0 = warp * spw;
     const int nnt = cdiv(it.ntok, 8);
+    const bool il = it.fmt == FMT_FP4;
+    const float fold = il ? 64.f : 1.f;  // FP4 weights enter the MMA as E2M1 x 2^-6
 #pragma unroll
     for (int nt = 0; nt < NTM; ++nt) {
         const int j = nt * 8 + g;
@@ -387,41 +462,56 @@ __device__ void load_b(const Item &it, int warp, int lane, int ue8m0, BRegs &B, 
             const bool sv = (sj < spw) && (s < nseg) && (nt < nnt);
             float sc = 0.f;
             if (sv) {
-                const int k0 = s * 128 + tig * 32;
                 if (it.bsrc == BS_PREQ) {
                     const uint8_t *src = tv ? (const uint8_t *)rowptr(it, j) : nullptr;
-                    codes32(src ? src + k0 : nullptr, tv, B.b[nt][sj]);
+                    codes_seg(src ? src + s * 128 : nullptr, tig, tv, il, B.b[nt][sj]);
                     sc = tv ? preq_scale(it, j, s) : 0.f;
                 } else {
                     const __nv_bfloat16 *src = tv ? (const __nv_bfloat16 *)rowptr(it, j) : nullptr;
-                    sc = quant32(tv ? src + k0 : nullptr, tv, ue8m0, B.b[nt][sj]);
+                    sc = quant_seg(tv ? src + s * 128 : nullptr, tig, tv, ue8m0, il, B.b[nt][sj]);
                 }
             } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) B.b[nt][sj][e] = 0u;
+                for (int e = 0; e < 8; ++e) B.b[nt][sj][e] = 0u;
             }
+            sc *= fold;
             B.sx[nt][sj][0] = __shfl_sync(0xffffffffu, sc, (2 * tig) * 4);
             B.sx[nt][sj][1] = __shfl_sync(0xffffffffu, sc, (2 * tig + 1) * 4);
         }
     }
 }
 
-// f16x2 {s, s} for an e8m0 scale byte (exact for bytes in [104, 140])
-__device__ __forceinline__ uint32_t scale_f16x2(uint32_t b) {
-    const __half h = __float2half_rn(e8m0_to_f32(b));
-    const uint32_t u = __half_as_ushort(h);
-    return u | (u << 16);
+// 8 packed E2M1 codes -> E4M3 bytes of value x 2^-6, split by element parity:
+// even elements (low nibbles) into `ev`, odd (high nibbles) into `od`.  An
+// E2M1 nibble s|e1 e0 m moved to bits s|.|.|.|e1 e0 m|.|. of a byte is the E4M3
+// encoding of its value x 2^-6, subnormal 0.5 included, so this is exact.
+__device__ __forceinline__ void fp4_to_e4m3(uint32_t w, uint32_t &ev, uint32_t &od) {
+    const uint32_t a = w << 2;  // low-nibble magnitude -> bits 4..2, its sign -> bit 5
+    ev = (a & 0x1c1c1c1cu) | ((a & 0x20202020u) << 2);
+    const uint32_t c = w >> 2;  // high-nibble magnitude -> bits 4..2, its sign -> bit 5
+    od = (c & 0x1c1c1c1cu) | ((c & 0x20202020u) << 2);
 }
 
 // FP8 block scale of global weight row `grow`, K-block `kb`
 template <typename FP8Scale>
 __device__ __forceinline__ float fp8_row_scale(const Item &it, int arow, int kb, FP8Scale f8s) {
-    const int run = arow / it.rrows;
-    const int grow = it.grow[run] + (arow - run * it.rrows);
+    const int run = arow >= it.rrows;
+    const int grow = (run ? it.grow[1] : it.grow[0]) + (arow - run * it.rrows);
     return f8s(grow / 128, it.kb0 + kb);
 }
 
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // One item's main loop for one consumer warp: acc[m][nt][c] over the warp's K segments.
+// Per 32-block j of segment s, lane (g, tig) supplies rows g and g+8, elements
+// 8*tig .. 8*tig+7 of the block (one 32-bit word of FP4, 8 bytes of FP8).
 template <typename FP8Scale>
 __device__ __forceinline__ void compute_item(const Item &it, const uint8_t *slot, int warp,
                                              int lane, const BRegs &B, float (&acc)[2][NTM][4],
@@ -446,28 +536,32 @@ __device__ __forceinline__ void compute_item(const Item &it, const uint8_t *slot
 #pragma unroll
                 for (int c = 0; c < 4; ++c) cs[nt][c] = 0.f;
             if (it.fmt == FMT_FP4) {
-                uint4 wa = make_uint4(0, 0, 0, 0), wb = wa;
-                uint32_t sa = 127, sbb = 127;
-                if (va) { wa = lds128(slot + ra * it.stride + s * 64 + tig * 16); sa = sc[ra * ks + s * 4 + tig]; }
-                if (vb) { wb = lds128(slot + rb * it.stride + s * 64 + tig * 16); sbb = sc[rb * ks + s * 4 + tig]; }
-                const uint32_t pa = scale_f16x2(sa), pb = scale_f16x2(sbb);
-                const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
-                const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+                // the 4 per-32 scales of this segment, one byte per block j
+                const uint32_t sa4 = va ? *reinterpret_cast<const uint32_t *>(sc + ra * ks + s * 4) : 0u;
+                const uint32_t sb4 = vb ? *reinterpret_cast<const uint32_t *>(sc + rb * ks + s * 4) : 0u;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t fa[4], fb[4];
-                    fp4x8_to_f16x8(wav[q], fa);
-                    fp4x8_to_f16x8(wbv[q], fb);
+                for (int j = 0; j < 4; ++j) {
+                    const int off = s * 64 + j * 16 + tig * 4;
+                    const uint32_t wa = va ? *reinterpret_cast<const uint32_t *>(slot + ra * it.stride + off) : 0u;
+                    const uint32_t wb = vb ? *reinterpret_cast<const uint32_t *>(slot + rb * it.stride + off) : 0u;
+                    uint32_t a0, a2, a1, a3;
+                    fp4_to_e4m3(wa, a0, a2);
+                    fp4_to_e4m3(wb, a1, a3);
+                    float d[NTM][4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) { fa[e] = hmul2_u32(fa[e], pa); fb[e] = hmul2_u32(fb[e], pb); }
+                    for (int nt = 0; nt < NTM; ++nt) {
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        const int j = 2 * q + jj;
+                        for (int c = 0; c < 4; ++c) d[nt][c] = 0.f;
+                        if (nt < nnt) mma_e4m3(d[nt], a0, a1, a2, a3, B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
+                    }
+                    const float fa = __uint_as_float(((sa4 >> (8 * j)) & 0xffu) << 23);
+                    const float fb = __uint_as_float(((sb4 >> (8 * j)) & 0xffu) << 23);
 #pragma unroll
-                        for (int nt = 0; nt < NTM; ++nt)
-                            if (nt < nnt)
-                                mma_f16(cs[nt], fa[2 * jj], fb[2 * jj], fa[2 * jj + 1], fb[2 * jj + 1],
-                                        B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
+                    for (int nt = 0; nt < NTM; ++nt) {
+                        cs[nt][0] = fmaf(d[nt][0], fa, cs[nt][0]);
+                        cs[nt][1] = fmaf(d[nt][1], fa, cs[nt][1]);
+                        cs[nt][2] = fmaf(d[nt][2], fb, cs[nt][2]);
+                        cs[nt][3] = fmaf(d[nt][3], fb, cs[nt][3]);
                     }
                 }
 #pragma unroll
@@ -478,31 +572,18 @@ __device__ __forceinline__ void compute_item(const Item &it, const uint8_t *slot
                     acc[m][nt][3] = fmaf(cs[nt][3], B.sx[nt][sj][1], acc[m][nt][3]);
                 }
             } else {
-                uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, b0 = a0, b1 = a0;
-                float fsa = 0.f, fsb = 0.f;
-                if (va) {
-                    const uint8_t *p = slot + ra * it.stride + s * 128 + tig * 32;
-                    a0 = lds128(p); a1 = lds128(p + 16);
-                    fsa = fp8_row_scale(it, ra, s, f8s);
-                }
-                if (vb) {
-                    const uint8_t *p = slot + rb * it.stride + s * 128 + tig * 32;
-                    b0 = lds128(p); b1 = lds128(p + 16);
-                    fsb = fp8_row_scale(it, rb, s, f8s);
-                }
-                const uint32_t wav[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const uint32_t wbv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t x0 = e4m3x2_to_f16x2((uint16_t)(wav[j] & 0xffffu));
-                    const uint32_t x2 = e4m3x2_to_f16x2((uint16_t)(wav[j] >> 16));
-                    const uint32_t x1 = e4m3x2_to_f16x2((uint16_t)(wbv[j] & 0xffffu));
-                    const uint32_t x3 = e4m3x2_to_f16x2((uint16_t)(wbv[j] >> 16));
+                for (int j = 0; j < 4; ++j) {
+                    const int off = s * 128 + j * 32 + tig * 8;
+                    uint2 wa = make_uint2(0, 0), wb = wa;
+                    if (va) wa = *reinterpret_cast<const uint2 *>(slot + ra * it.stride + off);
+                    if (vb) wb = *reinterpret_cast<const uint2 *>(slot + rb * it.stride + off);
 #pragma unroll
                     for (int nt = 0; nt < NTM; ++nt)
-                        if (nt < nnt)
-                            mma_f16(cs[nt], x0, x1, x2, x3, B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
+                        if (nt < nnt) mma_e4m3(cs[nt], wa.x, wb.x, wa.y, wb.y, B.b[nt][sj][2 * j], B.b[nt][sj][2 * j + 1]);
                 }
+                const float fsa = va ? fp8_row_scale(it, ra, s, f8s) : 0.f;
+                const float fsb = vb ? fp8_row_scale(it, rb, s, f8s) : 0.f;
 #pragma unroll
                 for (int nt = 0; nt < NTM; ++nt) {
                     acc[m][nt][0] = fmaf(cs[nt][0], fsa * B.sx[nt][sj][0], acc[m][nt][0]);
@@ -877,10 +958,11 @@ __device__ __forceinline__ void init_smem(const Smem &sm) {
 
 struct MoeRowPtr {
     const MoeArgs *a;
+    const int16_t *pair_tok;  // shared-memory copy (K2)
     __device__ const void *operator()(const Item &it, int j) const {
         const int p = it.tok0 + j;
         switch (it.bsrc) {
-            case BS_XPAIR: return a->x + (size_t)__ldg(a->pair_tok + p) * a->D;
+            case BS_XPAIR: return a->x + (size_t)pair_tok[p] * a->D;
             case BS_XTOK: return a->x + (size_t)p * a->D;
             case BS_H: return a->h + (size_t)p * a->I;
             default: return a->hs + (size_t)p * a->I;
@@ -901,7 +983,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     const int n = a.route_only ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
     int i0, i1;
     item_range(n, i0, i1);
-    auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0); };
+    auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0, nullptr, nullptr, nullptr); };
     if ((threadIdx.x >> 5) == NCW) {
         produce(sm, i0, i1, a.err, decode);
         return;
@@ -923,7 +1005,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
         }
         bar_sync(1, NCT);
     }
-    MoeRowPtr rp{&a};
+    MoeRowPtr rp{&a, nullptr};
     auto f8 = [&](int rblk, int kb) {
         const int kbs = a.D / 128;
         if (a.shared_f32) return __ldg((const float *)a.ss13 + rblk * kbs + kb);
@@ -947,15 +1029,23 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
     pdl_wait();
     pdl_launch_dependents();
     const int n_act = a.hdr[H_NACT], n_it2 = a.hdr[H_IT2];
+    load_route(sm, a.act_expert, a.act_off, a.act_it2, a.pair_tok, a.pair_w, n_act, a.hdr[H_NPAIR]);
+    const RouteSm rt = route_sm(sm);
     const int n = n_it2 + (a.D / a.g.rs2) * cdiv(a.T, TPI);
     int i0, i1;
     item_range(n, i0, i1);
-    auto decode = [&](int i) { return decode_moe(KID_MID, a, i, n_act, n_it2); };
+    auto decode = [&, c = Cursor{-1, 0}](int i) mutable {
+        if (i < n_it2) {
+            if (c.i < 0) c = cursor_at(rt, n_act, i);
+            while (c.i < i) cursor_next(rt, n_act, c);
+        }
+        return decode_moe(KID_MID, a, i, c.ai, n_it2, rt.act_expert, rt.act_off, rt.act_it);
+    };
     if ((threadIdx.x >> 5) == NCW) {
         produce(sm, i0, i1, a.err, decode);
         return;
     }
-    MoeRowPtr rp{&a};
+    MoeRowPtr rp{&a, rt.pair_tok};
     auto f8 = [&](int rblk, int kb) {
         const int kbs = a.I / 128;
         if (a.shared_f32) return __ldg((const float *)a.ss2 + rblk * kbs + kb);
@@ -968,7 +1058,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
                 const int tok = idx / nh, j = idx % nh;
                 const int p = it.tok0 + tok;
                 float hv = swiglu(red_sum(red, j, tok), red_sum(red, nh + j, tok), a.swiglu_limit);
-                hv = __ldg(a.pair_w + p) * hv;
+                hv = rt.pair_w[p] * hv;
                 a.h[(size_t)p * a.I + it.row0 + j] = __float2bfloat16_rn(hv);
             }
         } else {
@@ -996,14 +1086,20 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ Mo
         for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x) combine_rows(a, rb * a.g.r2, a.g.r2);
         return;
     }
+    load_route(sm, a.act_expert, a.act_off, a.act_it3, a.pair_tok, a.pair_w, n_act, a.hdr[H_NPAIR]);
+    const RouteSm rt = route_sm(sm);
     int i0, i1;
     item_range(n, i0, i1);
-    auto decode = [&](int i) { return decode_moe(KID_DOWN, a, i, n_act, 0); };
+    auto decode = [&, c = Cursor{-1, 0}](int i) mutable {
+        if (c.i < 0) c = cursor_at(rt, n_act, i);
+        while (c.i < i) cursor_next(rt, n_act, c);
+        return decode_moe(KID_DOWN, a, i, c.ai, 0, rt.act_expert, rt.act_off, rt.act_it);
+    };
     if ((threadIdx.x >> 5) == NCW) {
         produce(sm, i0, i1, a.err, decode);
         return;
     }
-    MoeRowPtr rp{&a};
+    MoeRowPtr rp{&a, rt.pair_tok};
     auto f8 = [&](int, int) { return 0.f; };
     volatile int *flag = sm.flags() + 1;
     auto epi = [&](const Item &it, const float *red, int tid) {
@@ -1159,7 +1255,7 @@ __global__ void k_scale_range(const uint8_t *s, long long n, int *bad) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         const uint8_t b = s[i];
-        if (b < 104 || b > 140) { atomicOr(bad, 1); return; }
+        if (b == 0 || b == 255) { atomicOr(bad, 1); return; }
     }
 }
 
@@ -1214,10 +1310,11 @@ int ensure_attrs() {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// smem row stride: row bytes rounded up to 128, plus 64 (FP4) or 16 (FP8) so
-// that the consumer warps' 16-byte loads of 8 rows fall in distinct banks
-int stride_fp4(int K) { return ((K / 2 + 127) / 128) * 128 + 64; }
-int stride_fp8(int K) { return ((K + 127) / 128) * 128 + 16; }
+// smem row stride: row bytes rounded up to 128, plus 16 (FP4: a warp reads one
+// 4-byte word from each of 8 rows x 4 lanes) or 32 (FP8: 8 bytes from 8 rows x
+// 4 lanes, two half-warp phases), so every access pattern is bank-conflict free
+int stride_fp4(int K) { return ((K / 2 + 127) / 128) * 128 + 16; }
+int stride_fp8(int K) { return ((K + 127) / 128) * 128 + 32; }
 
 int rows_fit(int stride) {
     int r = wf::SLOT_W / stride;

@@ -109,8 +109,7 @@ class MoELayer:
                 if ok < 0:
                     L.check(ok, "wf_fp4_scales_in_range")
                 if ok == 0:
-                    raise WfUnsupported("FP4 weight scales outside 2^-23..2^13 (e8m0 bytes 104..140), "
-                                        "where the f16 prescale of E2M1 values is not exact")
+                    raise WfUnsupported("FP4 weight scales contain e8m0 byte 0 (2^-127) or 255 (NaN)")
 
     def _check_shapes(self):
         w, D, I = self.weights, self.dim, self.inter_dim
