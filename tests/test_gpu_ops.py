@@ -17,6 +17,13 @@ def _ops():
     return ops
 
 
+@pytest.fixture(params=["tcgen05", "mma_sync"])
+def engine(request, monkeypatch):
+    """Dense GEMMs run on the tcgen05 kernel when shapes allow; WF_DISABLE_TC selects the other one."""
+    monkeypatch.setenv("WF_DISABLE_TC", "1" if request.param == "mma_sync" else "0")
+    return request.param
+
+
 def test_act_quant_bit_exact():
     ops = _ops()
     g = G.load("ops")
@@ -39,7 +46,7 @@ def test_fp4_act_quant_bit_exact(shape, std):
     assert np.array_equal(s.view(torch.uint8).cpu().numpy(), s_ref)
 
 
-def test_fp8_gemm_golden():
+def test_fp8_gemm_golden(engine):
     ops = _ops()
     g = G.load("ops")
     a = U.bf16_tensor(F.normal_bf16((103, 0), (4, 512), 1.0))
@@ -56,7 +63,7 @@ def test_fp8_gemm_golden():
     U.assert_layer_close(U.to_f32(c32), O.bf16_to_f32(g["op_fp8_gemm_fp32"]["c"]), "fp8 f32")
 
 
-def test_fp4_gemm_golden():
+def test_fp4_gemm_golden(engine):
     ops = _ops()
     g = G.load("ops")
     a = U.bf16_tensor(F.normal_bf16((103, 0), (4, 512), 1.0))
@@ -72,7 +79,7 @@ def test_fp4_gemm_golden():
                                    (3, 512, 2048), (9, 2048, 1024), (4, 4096, 16384), (16, 1024, 8192),
                                    (8, 129280, 4096), (1, 32768, 1024)])
 @pytest.mark.parametrize("scale", ["e8m0", "f32"])
-def test_fp8_gemm_vs_oracle(M, N, K, scale):
+def test_fp8_gemm_vs_oracle(M, N, K, scale, engine):
     """BASELINE config 3 shapes with K <= 4096 (fp32 weight scales per 128x128)."""
     ops = _ops()
     a16 = F.normal_bf16((201, M, N, K), (M, K), 1.0)
@@ -94,7 +101,7 @@ def test_fp8_gemm_vs_oracle(M, N, K, scale):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 4096, 8192), (12, 2048, 2048)])
-def test_fp4_gemm_vs_oracle(M, N, K):
+def test_fp4_gemm_vs_oracle(M, N, K, engine):
     """fp4_gemm (torch_ops.py:102-108), including split-K (K > 4096)."""
     ops = _ops()
     a16 = F.normal_bf16((211, M, N, K), (M, K), 1.0)

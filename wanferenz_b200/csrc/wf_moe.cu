@@ -28,10 +28,12 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/wfb200.h"
 #include "wf_ptx.cuh"
+#include "wf_tc.cuh"
 
 namespace wf {
 
@@ -1304,11 +1306,56 @@ int ensure_attrs() {
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, wf::SMEM_BYTES);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     }
+    cudaError_t e = cudaFuncSetAttribute((const void *)wf::tc::k_dense_tc,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, wf::tc::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc)");
     d.attr_done = true;
     return WF_OK;
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Tensor map of a [rows, K] weight matrix (FP4 packed or FP8), box 128 K x 128 rows,
+// 128-byte swizzle; FP4 is unpacked to one byte per element in shared memory.
+int weight_tensor_map(CUtensorMap *m, const void *base, bool fp4, uint64_t rows, uint64_t K,
+                      uint32_t box_rows = 128) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(WF_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {fp4 ? K / 2 : K};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                     const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WF_E_SHAPE, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return WF_OK;
+}
+
+bool tc_disabled() {
+    const char *v = getenv("WF_DISABLE_TC");
+    return v && v[0] && v[0] != '0';
+}
 
 // smem row stride: row bytes rounded up to 128, plus 16 (FP4: a warp reads one
 // 4-byte word from each of 8 rows x 4 lanes) or 32 (FP8: 8 bytes from 8 rows x
@@ -1643,6 +1690,26 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     if (ws_bytes < L.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
     int rc = ensure_attrs();
     if (rc) return rc;
+    // tcgen05 block-scaled path: UE8M0 scales on both sides, 128-row weight tiles
+    const bool tc_ok = !tc_disabled() && G == 0 && a_kind == WF_SCALE_E8M0 && b_kind == WF_SCALE_E8M0 &&
+                       N % 128 == 0 && (K / nkc) <= wf::tc::KC_MAX && ((uintptr_t)b % 32) == 0;
+    if (tc_ok) {
+        wf::tc::DenseArgs t;
+        memset(&t, 0, sizeof(t));
+        rc = weight_tensor_map(&t.tmA, b, wfmt == wf::FMT_FP4, (uint64_t)N, (uint64_t)K);
+        if (rc) return rc;
+        t.a = (const uint8_t *)a; t.a_s = (const uint8_t *)a_s; t.w_s = (const uint8_t *)b_s;
+        t.fp4 = wfmt == wf::FMT_FP4; t.M = (int)M; t.N = (int)N; t.K = (int)K;
+        t.nkc = nkc; t.Kc = (int)(K / nkc);
+        t.out = (__nv_bfloat16 *)out; t.err = (int *)ws;
+        t.cnt = (unsigned *)((uint8_t *)ws + L.cnt);
+        t.part = (float *)((uint8_t *)ws + L.part);
+        const int G_ = sm_count();
+        if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
+        wf::tc::k_dense_tc<<<G_, wf::tc::THREADS, wf::tc::SMEM, st>>>(t);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? WF_OK : cuda_fail(e, "tc gemm launch");
+    }
     wf::DenseArgs d;
     d.M = (int)M; d.N = (int)N; d.K = (int)K; d.G = (int)G;
     d.wfmt = wfmt; d.a_f32 = a_kind == WF_SCALE_F32; d.b_f32 = b_kind == WF_SCALE_F32;
