@@ -124,6 +124,27 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
                          float *out_weights, int64_t *out_indices, void *workspace,
                          size_t workspace_bytes, void *stream, void *const *events);
 
+/* Size of the module-scope device scratch wf_moe_forward_noalloc uses. */
+#define WF_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* wf_moe_forward for callers that cannot allocate device memory: a caller
+ * whose memory belongs to another allocator with nothing to hand out at call
+ * time, or one that must not call into the CUDA allocator on its serving path
+ * (cudaMalloc may synchronize the whole device).  The caller passes inputs and
+ * outputs only; the scratch is a 4 MiB array in this library's device module
+ * (WF_NOALLOC_SCRATCH_BYTES), which every device that loads the library keeps
+ * until the process exits.  A T whose scratch would exceed it (about 48 tokens
+ * at the V4-Flash shapes) is rejected with WF_E_SHAPE.  The first call on a
+ * device looks the array's device address up (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  Each call zeroes the array's counters
+ * (a cudaMemsetAsync on `stream`) and calls no allocator.  All calls on a
+ * device share the one array and it keeps the last call's contents, so calls
+ * that overlap on the GPU (other streams, other threads) race: order them on
+ * one stream.  No counterpart in the reference. */
+int wf_moe_forward_noalloc(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                           const int64_t *input_ids, int32_t T, void *y, float *out_weights,
+                           int64_t *out_indices, void *stream);
+
 /* Expert-parallel epilogue: y[t] = bf16(y_partial_reduced[t] + shared_out[row0 + t])
  * for t < T, where shared_out is the shared expert's output that the last
  * wf_moe_forward on this workspace left in it (architecture.py:791-794, after

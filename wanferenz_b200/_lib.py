@@ -23,7 +23,7 @@ EXPORTS = (
     "wf_moe_forward_timed",
     "wf_moe_finish", "wf_moe_route", "wf_moe_read_error", "wf_act_quant", "wf_fp4_act_quant",
     "wf_fp8_gemm", "wf_fp4_gemm", "wf_grouped_fp4_gemm", "wf_gemm_workspace_bytes",
-    "wf_fp4_scales_in_range",
+    "wf_fp4_scales_in_range", "wf_moe_forward_noalloc",
 )
 
 
@@ -81,6 +81,8 @@ def _declare(lib):
         "wf_grouped_fp4_gemm": (ctypes.c_int, [P, P, I32, P, P, I64, I64, I64, P, P, SZ, P]),
         "wf_gemm_workspace_bytes": (SZ, [I64, I64, I64]),
         "wf_fp4_scales_in_range": (ctypes.c_int, [P, I64, P]),
+        "wf_moe_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights),
+                                                  P, P, I32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

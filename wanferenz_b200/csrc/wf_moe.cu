@@ -1607,6 +1607,70 @@ int wf_moe_finish(const wf_moe_config *cfg, const float *yp, int32_t T, int32_t 
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "finish launch");
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free forward.  Some callers cannot give the layer a workspace:
+// their device memory is owned by another allocator that hands out nothing
+// at call time, or they may not call into the CUDA allocator on a
+// latency-critical path (cudaMalloc can synchronize the device).  For them
+// the scratch lives in this library's own module-scope device array, created
+// when the module loads on a device and held until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[WF_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_ptr[64];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  Host code may not use the array's name as an address.
+static int noalloc_scratch(void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(WF_E_CUDA, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return WF_OK;
+}
+
+int wf_moe_forward_noalloc(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                           const int64_t *input_ids, int32_t T, void *y, float *out_weights,
+                           int64_t *out_indices, void *stream) {
+    if (!cfg) return fail(WF_E_ARG, "null config");
+    if (T <= 0) return fail(WF_E_SHAPE, "T must be positive");
+    wf_moe_config c = *cfg;
+    c.max_tokens = T;  // size the scratch for this call only
+    int rc = check_cfg(&c);
+    if (rc) return rc;
+    const WsLayout L = ws_layout(&c);
+    if (L.total > WF_NOALLOC_SCRATCH_BYTES)
+        return fail(WF_E_SHAPE, "T too large for the static scratch of wf_moe_forward_noalloc (" +
+                                    std::to_string(L.total) + " bytes needed, " +
+                                    std::to_string((size_t)WF_NOALLOC_SCRATCH_BYTES) + " available)");
+    void *scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    wf::MoeArgs a;
+    rc = fill_args(&c, w, x, input_ids, T, scratch, WF_NOALLOC_SCRATCH_BYTES, a);
+    if (rc) return rc;
+    if (!y) return fail(WF_E_ARG, "null output");
+    if (!w->w13 || !w->w13_s || !w->w2 || !w->w2_s || !w->shared_w13 || !w->shared_s13 ||
+        !w->shared_w2 || !w->shared_s2)
+        return fail(WF_E_ARG, "null expert weight pointer");
+    // the error word and the completion counters must start at zero; the rest
+    // is fully written before it is read
+    cudaError_t e = cudaMemsetAsync(scratch, 0, L.logits, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch counters)");
+    a.y = (__nv_bfloat16 *)y; a.y_partial = nullptr; a.partial = 0;
+    a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    return launch_moe(a, false, (cudaStream_t)stream);
+}
+
 int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream) {
     if (!workspace || workspace_bytes < 16) return fail(WF_E_ARG, "null workspace");
     int host = 0;
