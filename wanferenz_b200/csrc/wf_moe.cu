@@ -1708,6 +1708,16 @@ int wf_fp4_act_quant(const void *x, int64_t M, int64_t K, void *q, void *s, void
 
 static int gemm_chunks(int64_t K) { return (int)((K + wf::KMAX - 1) / wf::KMAX); }
 
+// K chunks of the tcgen05 dense path: at least enough to fill ~2 items per SM
+// when there are few 128-row tiles, each chunk a multiple of 128 and <= 4096.
+static int tc_chunks(int64_t M, int64_t N, int64_t K) {
+    int nkc = gemm_chunks(K);
+    const int64_t items = ((M + 15) / 16) * (N / 128);
+    const int want = 2 * std::max(1, sm_count());
+    while (items * nkc < want && K % (128 * (nkc * 2)) == 0 && nkc < 16) nkc *= 2;
+    return nkc;
+}
+
 static int gemm_rows(int wfmt, int64_t N, int64_t K) {
     const int nkc = gemm_chunks(K);
     const int Kc = (int)(K / nkc);
@@ -1731,11 +1741,23 @@ static GemmWs gemm_ws(int64_t M, int64_t N, int64_t K, int rows) {
     return w;
 }
 
+// tcgen05 dense path: counters per (token group, 128-row tile, lane quadrant) + partials
+static GemmWs gemm_ws_tc(int64_t M, int64_t N, int64_t K, int nkc) {
+    GemmWs w{};
+    w.cnt = 256;
+    if (nkc <= 1) { w.part = w.total = 256; return w; }
+    w.part = w.cnt + align256((size_t)((M + 15) / 16) * (N / 128) * 4 * 4);
+    w.total = w.part + align256((size_t)nkc * M * N * 4);
+    return w;
+}
+
 size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0 || N % 8) return 0;
-    // sized for the finer of the FP8 / FP4 row blockings
+    // sized for the finer of the FP8 / FP4 row blockings, and for the tcgen05 split-K
     const int rows = std::min(gemm_rows(wf::FMT_FP8, N, K), gemm_rows(wf::FMT_FP4, N, K));
-    return gemm_ws(M, N, K, rows).total;
+    size_t need = gemm_ws(M, N, K, rows).total;
+    if (N % 128 == 0 && K % 128 == 0) need = std::max(need, gemm_ws_tc(M, N, K, tc_chunks(M, N, K)).total);
+    return need;
 }
 
 static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const void *b,
@@ -1758,16 +1780,23 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     const bool tc_ok = !tc_disabled() && G == 0 && a_kind == WF_SCALE_E8M0 && b_kind == WF_SCALE_E8M0 &&
                        N % 128 == 0 && (K / nkc) <= wf::tc::KC_MAX && ((uintptr_t)b % 32) == 0;
     if (tc_ok) {
+        const int tnkc = tc_chunks(M, N, K);
+        const GemmWs Lt = gemm_ws_tc(M, N, K, tnkc);
+        if (ws_bytes < Lt.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
+        if (tnkc > 1) {  // the workspace serves every shape: its counters start at zero per call
+            cudaError_t e0 = cudaMemsetAsync((uint8_t *)ws + Lt.cnt, 0, Lt.part - Lt.cnt, st);
+            if (e0 != cudaSuccess) return cuda_fail(e0, "cudaMemsetAsync(gemm counters)");
+        }
         wf::tc::DenseArgs t;
         memset(&t, 0, sizeof(t));
         rc = weight_tensor_map(&t.tmA, b, wfmt == wf::FMT_FP4, (uint64_t)N, (uint64_t)K);
         if (rc) return rc;
         t.a = (const uint8_t *)a; t.a_s = (const uint8_t *)a_s; t.w_s = (const uint8_t *)b_s;
         t.fp4 = wfmt == wf::FMT_FP4; t.M = (int)M; t.N = (int)N; t.K = (int)K;
-        t.nkc = nkc; t.Kc = (int)(K / nkc);
+        t.nkc = tnkc; t.Kc = (int)(K / tnkc);
         t.out = (__nv_bfloat16 *)out; t.err = (int *)ws;
-        t.cnt = (unsigned *)((uint8_t *)ws + L.cnt);
-        t.part = (float *)((uint8_t *)ws + L.part);
+        t.cnt = (unsigned *)((uint8_t *)ws + Lt.cnt);
+        t.part = (float *)((uint8_t *)ws + Lt.part);
         const int G_ = sm_count();
         if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
         wf::tc::k_dense_tc<<<G_, wf::tc::THREADS, wf::tc::SMEM, st>>>(t);
@@ -1784,6 +1813,10 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     d.rows = rows;
     d.cnt = (unsigned *)((uint8_t *)ws + L.cnt);
     d.part = (float *)((uint8_t *)ws + L.part);
+    if (nkc > 1) {  // the workspace serves every shape: its counters start at zero per call
+        cudaError_t e0 = cudaMemsetAsync((uint8_t *)ws + L.cnt, 0, L.part - L.cnt, st);
+        if (e0 != cudaSuccess) return cuda_fail(e0, "cudaMemsetAsync(gemm counters)");
+    }
     const int G_ = sm_count();
     if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
     wf::k_dense<<<G_, wf::NTHR, wf::SMEM_BYTES, st>>>(d);

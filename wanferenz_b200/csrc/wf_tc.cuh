@@ -103,6 +103,14 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Prefetch one 2D box of the tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 // ---- descriptors -------------------------------------------------------------
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
 // 1024 bytes (SBO), start address in 16-byte units, descriptor version 1.
@@ -362,9 +370,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
                 const int row = wt >> 3, chunk = wt & 7;
                 const bool rv = row < it.ntok;
                 const uint8_t *src = d.a + (size_t)(it.tok0 + (rv ? row : 0)) * K + (size_t)it.kc * d.Kc + chunk * 16;
-                for (int s = 0; s < nks; ++s) {
-                    uint4 v = rv ? ldg128(src + s * 128) : make_uint4(0, 0, 0, 0);
-                    *reinterpret_cast<uint4 *>(Bsm + s * BSTEP + sw128_offset(row, chunk)) = v;
+                for (int s0 = 0; s0 < nks; s0 += 8) {
+                    uint4 v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        v[u] = (rv && s0 + u < nks) ? ldg128(src + (s0 + u) * 128) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (s0 + u < nks)
+                            *reinterpret_cast<uint4 *>(Bsm + (s0 + u) * BSTEP + sw128_offset(row, chunk)) = v[u];
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 const bool tv = lane < it.ntok;
