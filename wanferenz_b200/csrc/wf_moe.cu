@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -101,6 +102,8 @@ struct MoeArgs {
     unsigned *cnt_router, *cnt_rb;
     int *err;
     Geo g;
+    int tc;              // expert phases on tcgen05 (k_moe_tc): K1 quantizes x, skips the shared expert
+    uint8_t *xq, *xs;    // E4M3 tokens [T, D] and their e8m0 scales [T, D/128] (tc)
 };
 
 // Dense GEMM (operator entry points) arguments.
@@ -921,11 +924,12 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
 // ---------------------------------------------------------------------------
 // combine of one output row block (K3): ascending-expert fp32 sum + shared
 // ---------------------------------------------------------------------------
+template <int NTH = NCT>
 __device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
     const int T = a.T, D = a.D, K = a.topk;
     const unsigned short *o = reinterpret_cast<const unsigned short *>(a.o);
     const unsigned short *os = reinterpret_cast<const unsigned short *>(a.os);
-    for (int idx = threadIdx.x; idx < T * nrows; idx += NCT) {
+    for (int idx = threadIdx.x; idx < T * nrows; idx += NTH) {
         const int t = idx / nrows, r = row0 + idx % nrows;
         float acc = 0.f;
         const int np = __ldcg(a.tok_np + t);
@@ -976,13 +980,37 @@ struct NoPreq {
     __device__ float operator()(const Item &, int, int) const { return 0.f; }
 };
 
+// act_quant (torch_ops.py:33-49) of the layer input for the tcgen05 expert
+// phases: token t by CTA t mod grid, one 128-block per warp at a time, four
+// elements per lane.  Scales are powers of two (ue8m0), stored as e8m0 bytes.
+__device__ void quantize_tokens(const MoeArgs &a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = a.D / 128;
+    for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+        for (int b = warp; b < nb; b += NCW) {
+            const uint2 u = __ldg(reinterpret_cast<const uint2 *>(a.x + (size_t)t * a.D + b * 128 + 4 * lane));
+            const float v0 = bf16_bits_to_f32(u.x & 0xffffu), v1 = bf16_bits_to_f32(u.x >> 16);
+            const float v2 = bf16_bits_to_f32(u.y & 0xffffu), v3 = bf16_bits_to_f32(u.y >> 16);
+            float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float s = round_scale_e8(fmaxf(m, 1e-4f), 1);
+            const float inv = 1.0f / s;  // exact: s is a power of two
+            auto q = [&](float v) { return fminf(fmaxf(v * inv, -448.f), 448.f); };
+            const uint32_t lo = f32x2_to_e4m3x2(q(v0), q(v1)), hi = f32x2_to_e4m3x2(q(v2), q(v3));
+            *reinterpret_cast<uint32_t *>(a.xq + (size_t)t * a.D + b * 128 + 4 * lane) = lo | (hi << 16);
+            if (lane == 0) a.xs[(size_t)t * nb + b] = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
     pdl_wait();
     pdl_launch_dependents();
-    const int n = a.route_only ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
+    const int n = (a.route_only || a.tc) ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0, nullptr, nullptr, nullptr); };
@@ -990,6 +1018,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
         produce(sm, i0, i1, a.err, decode);
         return;
     }
+    if (a.tc && !a.route_only) quantize_tokens(a);
     router_logits(a, sm);
     __threadfence();
     bar_sync(1, NCT);
@@ -1130,6 +1159,8 @@ __global__ void k_moe_finish(const float *yp, const __nv_bfloat16 *os, __nv_bflo
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         y[i] = __float2bfloat16_rn(yp[i] + __bfloat162float(os[i]));
 }
+
+#include "wf_moe_tc.cuh"
 
 __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ DenseArgs d) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1306,6 +1337,12 @@ int ensure_attrs() {
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, wf::SMEM_BYTES);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     }
+    const void *ts[] = {(const void *)wf::mtc::k_moe_tc<2>, (const void *)wf::mtc::k_moe_tc<3>};
+    for (const void *k : ts) {
+        cudaError_t e2 =
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, wf::mtc::SMEM);
+        if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFuncSetAttribute(moe tc)");
+    }
     cudaError_t e = cudaFuncSetAttribute((const void *)wf::tc::k_dense_tc,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, wf::tc::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc)");
@@ -1352,6 +1389,44 @@ int weight_tensor_map(CUtensorMap *m, const void *base, bool fp4, uint64_t rows,
     return WF_OK;
 }
 
+// Encoded tensor maps of the expert weights, cached by (pointer, shape):
+// weights stay in place between calls, and encoding costs host time.
+struct MapKey {
+    const void *base;
+    int dtype, rank;
+    uint64_t dims[3], strides[2];
+    uint32_t box[3];
+    bool operator<(const MapKey &o) const { return memcmp(this, &o, sizeof(MapKey)) < 0; }
+};
+std::mutex g_map_mu;
+std::map<MapKey, CUtensorMap> g_maps;
+
+int cached_map(CUtensorMap *out, bool fp4, int rank, const void *base, const uint64_t *dims,
+               const uint64_t *strides, const uint32_t *box) {
+    MapKey k;
+    memset(&k, 0, sizeof(k));
+    k.base = base; k.dtype = fp4; k.rank = rank;
+    for (int i = 0; i < rank; ++i) { k.dims[i] = dims[i]; k.box[i] = box[i]; }
+    for (int i = 0; i + 1 < rank; ++i) k.strides[i] = strides[i];
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    auto f = g_maps.find(k);
+    if (f != g_maps.end()) { *out = f->second; return WF_OK; }
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(WF_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t d[3], st[2];
+    cuuint32_t b[3], es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) { d[i] = dims[i]; b[i] = box[i]; }
+    for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+    CUresult r = enc(out, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, rank,
+                     const_cast<void *>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WF_E_SHAPE, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    if (g_maps.size() > 4096) g_maps.clear();
+    g_maps[k] = *out;
+    return WF_OK;
+}
+
 bool tc_disabled() {
     const char *v = getenv("WF_DISABLE_TC");
     return v && v[0] && v[0] != '0';
@@ -1368,10 +1443,23 @@ int rows_fit(int stride) {
     return r > wf::MAXR ? wf::MAXR : r;
 }
 
+// Grid bound of the tcgen05 expert phases (two stream-K partial slots per CTA).
+constexpr int TC_MAX_GRID = 256;
+
 struct WsLayout {
     size_t logits, hdr, act_expert, act_off, act_it2, act_it3, pair_tok, pair_w, tok_np,
         tok_pairs, ridx, rw, h, hs, o, os, cnt_router, cnt_rb, err, total;
+    // tcgen05 expert phases: counters (zeroed region) and buffers after `total`
+    size_t cnt_tc, xq, xs, hq, hqs, sq, sqs, part, total_tc;
 };
+
+// Upper bound of the items of one tcgen05 expert phase.
+size_t tc_max_items(const wf_moe_config *c) {
+    const size_t T = c->max_tokens, K = c->topk, El = c->n_local_experts;
+    const size_t nblk = std::max((size_t)c->inter_dim / 128, (size_t)c->dim / 256);
+    const size_t groups = (T + 15) / 16 + std::min(El, T * K) + (T * K + 15) / 16;
+    return groups * std::max<size_t>(nblk, 1);
+}
 
 WsLayout ws_layout(const wf_moe_config *c) {
     WsLayout L{};
@@ -1385,6 +1473,7 @@ WsLayout ws_layout(const wf_moe_config *c) {
     L.err = take(16);
     L.cnt_router = take(16);
     L.cnt_rb = take((size_t)(c->dim / 8 + 1) * 4);
+    L.cnt_tc = take(tc_max_items(c) * 4);
     L.hdr = take(wf::H_SIZE * 4);
     L.logits = take(T * E * 4);
     L.act_expert = take((El + 1) * 4);
@@ -1402,6 +1491,15 @@ WsLayout ws_layout(const wf_moe_config *c) {
     L.o = take(T * K * c->dim * 2);
     L.os = take(T * c->dim * 2);
     L.total = off;
+    const size_t D = c->dim, I = c->inter_dim;
+    L.xq = take(T * D);
+    L.xs = take(T * D / 128);
+    L.hq = take(T * K * I);
+    L.hqs = take(T * K * I / 128);
+    L.sq = take(T * I);
+    L.sqs = take(T * I / 128);
+    L.part = take((size_t)TC_MAX_GRID * 2 * (2 * 128 * wf::mtc::NT) * 4);
+    L.total_tc = off;
     return L;
 }
 
@@ -1449,8 +1547,58 @@ wf::Geo make_geo(int D, int I) {
     return g;
 }
 
+// Expert phases on tcgen05: needs power-of-two (e8m0) activation and shared
+// scales, 256-row output blocks, the tcgen05 workspace, aligned weight banks.
+int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, uint8_t *b,
+            size_t ws_bytes, wf::MoeArgs &a, wf::mtc::TcArgs *t) {
+    a.tc = 0;
+    if (!t || tc_disabled()) return WF_OK;
+    const int D = c->dim, I = c->inter_dim, El = c->n_local_experts;
+    if (!c->ue8m0 || w->shared_scale_kind == WF_SCALE_F32 || D % 256 || ws_bytes < L.total_tc) return WF_OK;
+    auto al = [](const void *p) { return ((uintptr_t)p & 255) == 0; };
+    if (!al(w->w13) || !al(w->w2) || !al(w->shared_w13) || !al(w->shared_w2)) return WF_OK;
+    memset(t, 0, sizeof(*t));
+    int rc;
+    {
+        const uint64_t dims[3] = {(uint64_t)D, (uint64_t)I, 2ull * El};
+        const uint64_t st[2] = {(uint64_t)D / 2, (uint64_t)I * D / 2};
+        const uint32_t box[3] = {128, 128, 2};
+        if ((rc = cached_map(&t->m_r13, true, 3, w->w13, dims, st, box))) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)D, (uint64_t)I, 2};
+        const uint64_t st[2] = {(uint64_t)D, (uint64_t)I * D};
+        const uint32_t box[3] = {128, 128, 2};
+        if ((rc = cached_map(&t->m_s13, false, 3, w->shared_w13, dims, st, box))) return rc;
+    }
+    {
+        const uint64_t dims[2] = {(uint64_t)I, (uint64_t)El * D};
+        const uint64_t st[1] = {(uint64_t)I / 2};
+        const uint32_t box[2] = {128, 256};
+        if ((rc = cached_map(&t->m_r2, true, 2, w->w2, dims, st, box))) return rc;
+    }
+    {
+        const uint64_t dims[2] = {(uint64_t)I, (uint64_t)D};
+        const uint64_t st[1] = {(uint64_t)I};
+        const uint32_t box[2] = {128, 256};
+        if ((rc = cached_map(&t->m_s2, false, 2, w->shared_w2, dims, st, box))) return rc;
+    }
+    a.tc = 1;
+    a.xq = b + L.xq; a.xs = b + L.xs;
+    t->xq = a.xq; t->xs = a.xs;
+    t->hq = b + L.hq; t->hqs = b + L.hqs;
+    t->sq = b + L.sq; t->sqs = b + L.sqs;
+    t->part = (float *)(b + L.part);
+    t->cnt = (unsigned *)(b + L.cnt_tc);
+    // items of 128 h-rows (w1/w3) and 256 output rows (w2) in the dispatch tables
+    a.g.nh13 = 128;
+    a.g.r2 = 256;
+    return WF_OK;
+}
+
 int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
-              const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a) {
+              const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a,
+              wf::mtc::TcArgs *t = nullptr) {
     int rc = check_cfg(c);
     if (rc) return rc;
     if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
@@ -1491,7 +1639,7 @@ int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
     a.cnt_rb = (unsigned *)(b + L.cnt_rb);
     a.err = (int *)(b + L.err);
     a.g = make_geo(a.D, a.I);
-    return WF_OK;
+    return fill_tc(c, w, L, b, ws_bytes, a, t);
 }
 
 }  // namespace
@@ -1504,16 +1652,17 @@ int wf_device_sm_count(void) { return sm_count(); }
 
 size_t wf_moe_workspace_bytes(const wf_moe_config *cfg) {
     if (check_cfg(cfg)) return 0;
-    return ws_layout(cfg).total;
+    return ws_layout(cfg).total_tc;
 }
 
 static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
-                      void *const *ev = nullptr) {
+                      void *const *ev = nullptr, const wf::mtc::TcArgs *t = nullptr) {
     int rc = ensure_attrs();
     if (rc) return rc;
-    const int G = sm_count();
+    int G = sm_count();
     if (G <= 0) return fail(WF_E_CUDA, "no CUDA device");
     a.route_only = route_only;
+    if (a.tc && !t) return fail(WF_E_ARG, "tcgen05 phases without their arguments");
     // Programmatic dependent launch: a kernel may begin launching while the one
     // before it drains; each kernel waits (griddepcontrol.wait) before reading
     // anything an earlier kernel wrote.  Event records break the overlap on
@@ -1528,6 +1677,10 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
     lc.stream = st;
     lc.attrs = attr;
     lc.numAttrs = 1;
+    cudaLaunchConfig_t lt = lc;
+    lt.gridDim = dim3(std::min(G, TC_MAX_GRID));
+    lt.blockDim = dim3(wf::mtc::THREADS);
+    lt.dynamicSmemBytes = wf::mtc::SMEM;
     cudaError_t e = cudaSuccess;
     auto rec = [&](int i) {
         if (ev && e == cudaSuccess)
@@ -1537,13 +1690,28 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
     if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_up, a);
     rec(1);
     if (!route_only) {
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_mid, a);
-        rec(2);
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_down, a);
-        rec(3);
+        if (a.tc) {
+            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<2>, a, *t);
+            rec(2);
+            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<3>, a, *t);
+            rec(3);
+        } else {
+            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_mid, a);
+            rec(2);
+            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_down, a);
+            rec(3);
+        }
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "MoE kernel launch");
+    return WF_OK;
+}
+
+static int check_expert_ptrs(const wf_moe_weights *w) {
+    if (!w) return fail(WF_E_ARG, "null weights");
+    if (!w->w13 || !w->w13_s || !w->w2 || !w->w2_s || !w->shared_w13 || !w->shared_s13 ||
+        !w->shared_w2 || !w->shared_s2)
+        return fail(WF_E_ARG, "null expert weight pointer");
     return WF_OK;
 }
 
@@ -1551,16 +1719,16 @@ int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void
                    const int64_t *input_ids, int32_t T, void *y, float *y_partial,
                    float *out_weights, int64_t *out_indices, void *workspace,
                    size_t workspace_bytes, void *stream) {
+    int rc = check_expert_ptrs(w);
+    if (rc) return rc;
     wf::MoeArgs a;
-    int rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a);
+    wf::mtc::TcArgs t;
+    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
-    if (!w->w13 || !w->w13_s || !w->w2 || !w->w2_s || !w->shared_w13 || !w->shared_s13 ||
-        !w->shared_w2 || !w->shared_s2)
-        return fail(WF_E_ARG, "null expert weight pointer");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
-    return launch_moe(a, false, (cudaStream_t)stream);
+    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
 }
 
 int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
@@ -1570,13 +1738,16 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
     if (!events) return fail(WF_E_ARG, "null events");
     for (int i = 0; i < 4; ++i)
         if (!events[i]) return fail(WF_E_ARG, "null event");
+    int rc = check_expert_ptrs(w);
+    if (rc) return rc;
     wf::MoeArgs a;
-    int rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a);
+    wf::mtc::TcArgs t;
+    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
-    return launch_moe(a, false, (cudaStream_t)stream, events);
+    return launch_moe(a, false, (cudaStream_t)stream, events, &t);
 }
 
 int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,

@@ -1,0 +1,617 @@
+// wf_moe_tc.cuh - the expert phases of the MoE layer on the 5th-generation
+// tensor cores (tcgen05), included by wf_moe.cu inside namespace wf.
+//
+//   phase 2 (w1/w3): h = act_quant(weights * silu(x W1^T) * (x W3^T))  per expert
+//   phase 3 (w2):    o = h W2^T per expert, then the ascending-expert combine
+//
+// reference: Expert.forward (architecture.py:728-741) on fp4_gemm / fp8_gemm
+// (torch_ops.py:93-108), MoE.forward's combine (architecture.py:785-794).
+//
+// Work list.  An item is one token group (<= 16 tokens of one expert, or of
+// the shared expert) times one weight row block: for phase 2 the 128 gate rows
+// and the matching 128 up rows (one h quantization block), for phase 3 256
+// output rows.  Shared-expert items come first, then the routed items in
+// ascending local expert order (tables written by the router kernel).  Every
+// item has the same number of 128-wide K steps, and the grid splits the
+// concatenated K steps of all items evenly (stream-K): a CTA owns the
+// contiguous range [S*b/G, S*(b+1)/G).  An item cut by a range boundary
+// leaves fp32 partials in per-CTA slots; the last of its segments to finish
+// (arrival counter) sums them in segment order, so the result does not depend
+// on timing.
+//
+// One K step = one 32 KB shared-memory stage: 256 weight rows x 128 K, one
+// byte per element (FP4 E2M1 is unpacked by TMA type 16U4_ALIGN16B, FP8 E4M3
+// is copied as is), 128-byte swizzle, as two M = 128 tiles.
+//
+// Warp roles (224 threads):
+//   warps 0-3  workers: B operand (the item's tokens as E4M3, all K steps) in
+//              shared memory, B scales and weight scales in TMEM, epilogue
+//              (TMEM -> registers, SwiGLU + quantization or bf16 output)
+//   warp 4     TMA producer of the weight stages
+//   warps 5-6  MMA issuers: issuer i issues the steps of local parity i of a
+//              segment into its own accumulators (one thread issuing block-
+//              scaled MMAs back to back is the throughput limit, two are not)
+#pragma once
+
+namespace mtc {
+
+constexpr int W_PROD = 4, W_ISS0 = 5, NISS = 2;
+constexpr int THREADS = 7 * 32;
+constexpr int NWK = 128;                 // worker threads
+constexpr int STAGES = 4;
+constexpr int STAGE_BYTES = 32768;
+constexpr int TILE_BYTES = 16384;
+constexpr int NT = 16;                   // tokens per item (MMA N)
+constexpr int BSTEP = NT * 128;          // B bytes per K step
+constexpr int MAX_STEPS = 32;            // K <= 4096
+constexpr int GRP = 8;                   // K steps per weight-scale group
+constexpr int OFF_A = 0;
+constexpr int OFF_B = STAGES * STAGE_BYTES;
+constexpr int OFF_BAR = OFF_B + MAX_STEPS * BSTEP;
+constexpr int NBAR = 2 * STAGES + 12;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int OFF_EX = OFF_MISC + 64;            // [4 warps][NT] amax exchange
+constexpr int OFF_ROUTE = OFF_EX + 4 * NT * 4;   // act_expert, act_off, act_it
+constexpr int ROUTE_BYTES = 3 * (MAX_E + 1) * 4;
+constexpr int SMEM = OFF_ROUTE + ROUTE_BYTES + 1024;  // + alignment slack
+static_assert(SMEM <= 232448, "shared memory budget");
+// TMEM columns (512 allocated)
+constexpr uint32_t COL_D = 0;      // [issuer][buf][tile] x NT
+constexpr uint32_t COL_SFB = 128;  // [K step] x 4
+constexpr uint32_t COL_SFA = 256;  // [group buf][step in group][tile] x 4
+static_assert(COL_D + NISS * 2 * 2 * NT <= COL_SFB, "accumulator columns");
+static_assert(COL_SFB + MAX_STEPS * 4 <= COL_SFA, "B scale columns");
+static_assert(COL_SFA + 2 * GRP * 2 * 4 <= 512, "weight scale columns");
+
+struct TcArgs {
+    CUtensorMap m_r13;  // routed w1/w3, FP4, 3D {D, I, 2E}: box 128 x 128 x 2 (gate, up)
+    CUtensorMap m_s13;  // shared w1/w3, FP8, 3D {D, I, 2}: box 128 x 128 x 2
+    CUtensorMap m_r2;   // routed w2, FP4, 2D {I, E*D}: box 128 x 256
+    CUtensorMap m_s2;   // shared w2, FP8, 2D {I, D}: box 128 x 256
+    const uint8_t *xq, *xs;    // tokens E4M3 [T, D], e8m0 [T, D/128] (router kernel)
+    uint8_t *hq, *hqs;         // routed hidden E4M3 [P, I], e8m0 [P, I/128]
+    uint8_t *sq, *sqs;         // shared hidden E4M3 [T, I], e8m0 [T, I/128]
+    float *part;               // [2 * grid][2][128][NT] partial slots
+    unsigned *cnt;             // [items] segment arrivals
+};
+
+struct Bars {
+    uint64_t *full, *empty, *b_ready, *b_free, *sfa_ready, *sfa_free, *d_ready, *d_free, *fin;
+};
+
+__device__ __forceinline__ Bars bars_at(uint8_t *base) {
+    uint64_t *b = reinterpret_cast<uint64_t *>(base + OFF_BAR);
+    Bars r;
+    r.full = b;
+    r.empty = b + STAGES;
+    r.b_ready = b + 2 * STAGES;
+    r.b_free = b + 2 * STAGES + 1;
+    r.sfa_ready = b + 2 * STAGES + 2;  // [2]
+    r.sfa_free = b + 2 * STAGES + 4;   // [2]
+    r.d_ready = b + 2 * STAGES + 6;    // [2]
+    r.d_free = b + 2 * STAGES + 8;     // [2]
+    r.fin = b + 2 * STAGES + 10;       // [2] issuer drain
+    return r;
+}
+
+// Item of phase PH (2: w1/w3, 3: w2).
+struct TItem {
+    int shared, el, blk, tok0, ntok, key;
+};
+
+struct TRoute {
+    const int *act_expert, *act_off, *act_it;
+    int n_act, ns, nblk;
+};
+
+// Walks items in increasing order (each role keeps its own).
+struct TCursor {
+    int ai = 0;
+    bool init = false;
+};
+
+template <int PH>
+__device__ __forceinline__ TItem decode(const MoeArgs &a, const TRoute &r, TCursor &c, int i) {
+    TItem it;
+    if (i < r.ns) {
+        const int tg = i / r.nblk;
+        it.shared = 1; it.el = 0; it.blk = i - tg * r.nblk;
+        it.tok0 = tg * NT; it.ntok = min(NT, a.T - it.tok0);
+    } else {
+        const int j = i - r.ns;
+        if (!c.init) {
+            int lo = 0, hi = r.n_act - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (r.act_it[mid] <= j) lo = mid; else hi = mid - 1;
+            }
+            c.ai = lo;
+            c.init = true;
+        }
+        while (c.ai + 1 < r.n_act && j >= r.act_it[c.ai + 1]) ++c.ai;
+        const int local = j - r.act_it[c.ai];
+        const int tg = local / r.nblk;
+        const int p0 = r.act_off[c.ai], ta = r.act_off[c.ai + 1] - p0;
+        it.shared = 0; it.el = r.act_expert[c.ai] - a.e0; it.blk = local - tg * r.nblk;
+        it.tok0 = p0 + tg * NT; it.ntok = min(NT, ta - tg * NT);
+    }
+    it.key = i / r.nblk;
+    return it;
+}
+
+// CTA owning K step x of the S steps split over G CTAs
+__device__ __forceinline__ int cta_of(long long x, long long S, int G) {
+    return (int)(((x + 1) * G - 1) / S);
+}
+__device__ __forceinline__ long long cta_start(int b, long long S, int G) { return S * b / G; }
+
+__device__ __forceinline__ bool twait(uint64_t *bar, uint32_t parity, int *err, volatile int *abort) {
+    if (*abort) return false;
+    if (!wf_wait(bar, parity, err)) { *abort = 1; return false; }
+    return true;
+}
+
+// OR of `v` over the `n` threads of named barrier `id` (every one of them must call it)
+__device__ __forceinline__ int bar_or(int id, int n, int v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(v), "r"(id), "r"(n)
+        : "memory");
+    return r;
+}
+
+__device__ __forceinline__ uint8_t e4m3_byte(float v) {
+    return (uint8_t)(f32x2_to_e4m3x2(v, 0.f) & 0xffu);
+}
+
+// Segment of one CTA's range: item i, K steps [j0, j1), its ordinal q.
+struct Seg {
+    int i, j0, j1, q;
+};
+
+template <int PH>
+__global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ MoeArgs a,
+                                                       const __grid_constant__ TcArgs t) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const Bars B = bars_at(base);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base + OFF_MISC);
+    volatile int *abort = reinterpret_cast<volatile int *>(base + OFF_MISC) + 1;
+    volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_MISC) + 2;
+    float *ex = reinterpret_cast<float *>(base + OFF_EX);
+    int *rt_s = reinterpret_cast<int *>(base + OFF_ROUTE);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, 1); }
+        mbar_init(B.b_ready, 4);
+        mbar_init(B.b_free, NISS);
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(B.sfa_ready + j, 4); mbar_init(B.sfa_free + j, NISS);
+            mbar_init(B.d_ready + j, NISS); mbar_init(B.d_free + j, 4);
+            mbar_init(B.fin + j, 1);
+        }
+        *abort = 0;
+        *flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == W_PROD) { tc::tmem_alloc(tmem_slot, 512); tc::tmem_relinquish(); }
+    // everything below reads what the previous kernel wrote
+    pdl_wait();
+    pdl_launch_dependents();
+    const int n_act = a.hdr[H_NACT];
+    TRoute r;
+    {
+        const int *src_it = PH == 2 ? a.act_it2 : a.act_it3;
+        for (int k = threadIdx.x; k <= n_act; k += THREADS) {
+            rt_s[k] = k < n_act ? a.act_expert[k] : 0;
+            rt_s[(MAX_E + 1) + k] = a.act_off[k];
+            rt_s[2 * (MAX_E + 1) + k] = src_it[k];
+        }
+        r.act_expert = rt_s;
+        r.act_off = rt_s + (MAX_E + 1);
+        r.act_it = rt_s + 2 * (MAX_E + 1);
+        r.n_act = n_act;
+        r.nblk = PH == 2 ? a.I / 128 : a.D / 256;
+        r.ns = r.nblk * cdiv(a.T, NT);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tm = *tmem_slot;
+
+    const int D = a.D, I = a.I;
+    const int K = PH == 2 ? D : I;
+    const int nst = K / 128;
+    const int n_items = r.ns + (PH == 2 ? a.hdr[H_IT2] : a.hdr[H_IT3]);
+    const long long S = (long long)n_items * nst;
+    const int G = gridDim.x;
+    const long long u0 = cta_start(blockIdx.x, S, G), u1 = cta_start(blockIdx.x + 1, S, G);
+    // segment after `sg` (or the first one when sg.q < 0); false at the end of the range
+    auto next_seg = [&](Seg &sg) -> bool {
+        const long long u = sg.q < 0 ? u0 : (long long)sg.i * nst + sg.j1;
+        if (u >= u1) return false;
+        sg.i = (int)(u / nst);
+        sg.j0 = (int)(u - (long long)sg.i * nst);
+        sg.j1 = (int)min((long long)nst, sg.j0 + (u1 - u));
+        sg.q += 1;
+        return true;
+    };
+
+    if (warp == W_PROD) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            TCursor cur;
+            Seg sg{0, 0, 0, -1};
+            int gs = 0;
+            while (!*abort && next_seg(sg)) {
+                const TItem it = decode<PH>(a, r, cur, sg.i);
+                const uint32_t tx = it.shared ? STAGE_BYTES : STAGE_BYTES / 2;
+                for (int j = sg.j0; j < sg.j1; ++j, ++gs) {
+                    const int st = gs & (STAGES - 1);
+                    if (gs >= STAGES && !twait(B.empty + st, ((gs / STAGES) - 1) & 1, a.err, abort)) break;
+                    uint8_t *dst = base + OFF_A + st * STAGE_BYTES;
+                    mbar_arrive_expect_tx(B.full + st, tx);
+                    if (PH == 2) {
+                        if (it.shared) tc::tma_load_3d(dst, &t.m_s13, j * 128, it.blk * 128, 0, B.full + st);
+                        else tc::tma_load_3d(dst, &t.m_r13, j * 128, it.blk * 128, 2 * it.el, B.full + st);
+                    } else {
+                        if (it.shared) tc::tma_load_2d(dst, &t.m_s2, j * 128, it.blk * 256, B.full + st);
+                        else tc::tma_load_2d(dst, &t.m_r2, j * 128, it.el * D + it.blk * 256, B.full + st);
+                    }
+                }
+            }
+            // every issued copy lands before the CTA may exit
+            for (int k = 0; k < STAGES && k < gs; ++k) {
+                const int g = gs - 1 - k, st = g & (STAGES - 1);
+                wf_wait(B.full + st, (g / STAGES) & 1, a.err);
+            }
+        }
+    } else if (warp >= W_ISS0) {
+        // ------------------------------------------------------------ MMA issuers
+        const int ii = warp - W_ISS0;
+        if (lane == 0) {
+            TCursor cur;
+            Seg sg{0, 0, 0, -1};
+            int gs = 0, gi = 0, nb = 0, key = -1;
+            const uint64_t a0 = tc::smem_desc_sw128(base + OFF_A);
+            const uint64_t b0 = tc::smem_desc_sw128(base + OFF_B);
+            bool more = next_seg(sg);
+            while (more && !*abort) {
+                const TItem it = decode<PH>(a, r, cur, sg.i);
+                const int buf = sg.q & 1;
+                if (it.key != key) {
+                    if (!twait(B.b_ready, nb & 1, a.err, abort)) break;
+                    ++nb;
+                    key = it.key;
+                }
+                if (sg.q >= 2 && !twait(B.d_free + buf, ((sg.q >> 1) - 1) & 1, a.err, abort)) break;
+                tc::fence_after_sync();
+                const int afmt = it.shared ? 0 : 5;
+                const uint32_t id0 = tc::idesc_mxf8f6f4(afmt, 0, NT, 0), id1 = tc::idesc_mxf8f6f4(afmt, 0, NT, 1);
+                const uint32_t id2 = tc::idesc_mxf8f6f4(afmt, 0, NT, 2), id3 = tc::idesc_mxf8f6f4(afmt, 0, NT, 3);
+                const uint32_t dcol = tm + COL_D + (uint32_t)((ii * 2 + buf) * 2 * NT);
+                bool first = true;
+                bool ok = true;
+                for (int j = sg.j0; j < sg.j1; ++j, ++gs) {
+                    const int jj = j - sg.j0;
+                    const int gj = jj & (GRP - 1);
+                    if (gj == 0) {
+                        if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort)) { ok = false; break; }
+                    }
+                    if ((jj & 1) == ii) {
+                        const int st = gs & (STAGES - 1);
+                        if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
+                        tc::fence_after_sync();
+                        const uint64_t ad = a0 + (uint64_t)((st * STAGE_BYTES) >> 4);
+                        const uint64_t bd = b0 + (uint64_t)((j * BSTEP) >> 4);
+                        const uint32_t sfa = tm + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8) + gj * 8);
+                        const uint32_t sfb = tm + COL_SFB + (uint32_t)(4 * j);
+#pragma unroll
+                        for (int tt = 0; tt < 2; ++tt) {
+                            const uint64_t at = ad + (uint64_t)((tt * TILE_BYTES) >> 4);
+                            const uint32_t dc = dcol + (uint32_t)(tt * NT), sa = sfa + (uint32_t)(4 * tt);
+                            tc::mma_mxf8f6f4(dc, at + 0, bd + 0, id0, sa, sfb, first ? 0u : 1u);
+                            tc::mma_mxf8f6f4(dc, at + 2, bd + 2, id1, sa, sfb, 1u);
+                            tc::mma_mxf8f6f4(dc, at + 4, bd + 4, id2, sa, sfb, 1u);
+                            tc::mma_mxf8f6f4(dc, at + 6, bd + 6, id3, sa, sfb, 1u);
+                        }
+                        first = false;
+                        tc::commit(B.empty + st);
+                    }
+                    if (gj == GRP - 1 || j == sg.j1 - 1) {
+                        tc::commit(B.sfa_free + (gi & 1));
+                        ++gi;
+                    }
+                }
+                if (!ok) break;
+                tc::commit(B.d_ready + buf);
+                const int key_now = it.key;
+                more = next_seg(sg);
+                // the B operand may be replaced once this token set's MMAs are done
+                if (!more || (sg.i / r.nblk) != key_now) tc::commit(B.b_free);
+            }
+            // all of this thread's MMAs complete before TMEM is released
+            tc::commit(B.fin + ii);
+            wf_wait(B.fin + ii, 0, a.err);
+        }
+    } else {
+        // ------------------------------------------------------------ workers
+        const int wq = warp;  // TMEM lane quadrant
+        const int tid = threadIdx.x;
+        const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
+        const int row = 32 * wq + lane;  // accumulator lane = row within a 128-row tile
+        TCursor cur, cur_e;
+        Seg sg{0, 0, 0, -1};
+        int gi = 0, nb = 0, key = -1;
+        uint8_t *Bsm = base + OFF_B;
+        // The four worker warps share named barriers, so each wait ends in one
+        // decision for all of them: a timeout seen by any warp stops every warp.
+        bool dead = false;
+        auto wwait = [&](uint64_t *bar, uint32_t parity) -> bool {
+            const bool ok = twait(bar, parity, a.err, abort);
+            if (bar_or(1, NWK, !ok)) dead = true;
+            return !dead;
+        };
+
+        auto epilogue = [&](const Seg &e) {
+            const TItem it = decode<PH>(a, r, cur_e, e.i);
+            const int buf = e.q & 1;
+            if (!wwait(B.d_ready + buf, (e.q >> 1) & 1)) return;
+            tc::fence_after_sync();
+            uint32_t v0[NT], v1[NT], w0[NT], w1[NT];
+            tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((0 * 2 + buf) * 2 * NT), v0);
+            tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((0 * 2 + buf) * 2 * NT + NT), v1);
+            const bool two = e.j1 - e.j0 >= 2;
+            if (two) {
+                tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((1 * 2 + buf) * 2 * NT), w0);
+                tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((1 * 2 + buf) * 2 * NT + NT), w1);
+            }
+            tc::tmem_wait_ld();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(B.d_free + buf);
+            float g[NT], u[NT];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                g[n] = __uint_as_float(v0[n]);
+                u[n] = __uint_as_float(v1[n]);
+                if (two) {
+                    g[n] += __uint_as_float(w0[n]);
+                    u[n] += __uint_as_float(w1[n]);
+                }
+            }
+            const int ntok = it.ntok;
+            if (!(e.j0 == 0 && e.j1 == nst)) {
+                // stream-K: this segment's partial sums go to the CTA's slot; the last
+                // segment of the item to arrive sums all of them in segment order
+                const long long is = (long long)e.i * nst;
+                const int mine = blockIdx.x * 2 + (u0 >= is ? 0 : 1);
+                float *ps = t.part + (size_t)mine * (2 * 128 * NT);
+#pragma unroll
+                for (int n = 0; n < NT; ++n)
+                    if (n < ntok) {
+                        ps[(0 * 128 + row) * NT + n] = g[n];
+                        ps[(1 * 128 + row) * NT + n] = u[n];
+                    }
+                __threadfence();
+                bar_sync(1, NWK);
+                if (tid == 0) {
+                    const int blo = cta_of(is, S, G), bhi = cta_of(is + nst - 1, S, G);
+                    int nseg = 0;
+                    for (int b = blo; b <= bhi; ++b)
+                        nseg += cta_start(b + 1, S, G) > cta_start(b, S, G);
+                    const unsigned old = atomicAdd(t.cnt + e.i, 1u);
+                    *flag = old == (unsigned)(nseg - 1);
+                }
+                bar_sync(1, NWK);
+                const int last = *flag;
+                bar_sync(1, NWK);
+                if (!last) return;
+                __threadfence();
+#pragma unroll
+                for (int n = 0; n < NT; ++n) { g[n] = 0.f; u[n] = 0.f; }
+                const int blo = cta_of(is, S, G), bhi = cta_of(is + nst - 1, S, G);
+                for (int b = blo; b <= bhi; ++b) {
+                    const long long ub = cta_start(b, S, G);
+                    if (cta_start(b + 1, S, G) <= ub) continue;
+                    const float *pp = t.part + (size_t)(b * 2 + (ub >= is ? 0 : 1)) * (2 * 128 * NT);
+#pragma unroll
+                    for (int n = 0; n < NT; ++n)
+                        if (n < ntok) {
+                            g[n] += __ldcg(pp + (0 * 128 + row) * NT + n);
+                            u[n] += __ldcg(pp + (1 * 128 + row) * NT + n);
+                        }
+                }
+                if (tid == 0) t.cnt[e.i] = 0u;
+            }
+            if (PH == 2) {
+                // SwiGLU (architecture.py:733-741) then act_quant of this 128-row block
+                float h[NT];
+                float am[NT];
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    float hv = 0.f;
+                    if (n < ntok) {
+                        hv = swiglu(g[n], u[n], a.swiglu_limit);
+                        if (!it.shared) hv = __ldg(a.pair_w + it.tok0 + n) * hv;
+                        hv = bf16r(hv);
+                    }
+                    h[n] = hv;
+                    float m = fabsf(hv);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    am[n] = m;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) ex[wq * NT + n] = am[n];
+                }
+                bar_sync(1, NWK);
+                uint8_t *dq = it.shared ? t.sq : t.hq;
+                uint8_t *ds = it.shared ? t.sqs : t.hqs;
+                const int ib = I / 128;
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    if (n >= ntok) continue;
+                    const float amax = fmaxf(fmaxf(ex[n], ex[NT + n]), fmaxf(ex[2 * NT + n], ex[3 * NT + n]));
+                    const float s = round_scale_e8(fmaxf(amax, 1e-4f), 1);
+                    const float inv = 1.0f / s;
+                    const float qv = fminf(fmaxf(h[n] * inv, -448.f), 448.f);
+                    const size_t prow = (size_t)(it.tok0 + n);
+                    dq[prow * I + it.blk * 128 + row] = e4m3_byte(qv);
+                    if (tid == 0) ds[prow * ib + it.blk] = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
+                }
+                bar_sync(1, NWK);  // the exchange buffer is reused by the next epilogue
+            } else {
+                __nv_bfloat16 *dst = it.shared ? a.os : a.o;
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    if (n >= ntok) continue;
+                    const size_t o = (size_t)(it.tok0 + n) * D + it.blk * 256 + row;
+                    dst[o] = __float2bfloat16_rn(g[n]);
+                    dst[o + 128] = __float2bfloat16_rn(u[n]);
+                }
+                // combine of this 256-row block once every token group has written it
+                __threadfence();
+                bar_sync(1, NWK);
+                if (tid == 0) {
+                    const unsigned target = (unsigned)(a.hdr[H_TGT] + cdiv(a.T, NT));
+                    const unsigned old = atomicAdd(a.cnt_rb + it.blk, 1u);
+                    *flag = old == target - 1;
+                }
+                bar_sync(1, NWK);
+                const int last = *flag;
+                bar_sync(1, NWK);
+                if (last) {
+                    __threadfence();
+                    combine_rows<NWK>(a, it.blk * 256, 256);
+                    if (tid == 0) a.cnt_rb[it.blk] = 0u;
+                }
+            }
+        };
+
+        Seg prev{0, 0, 0, -1};
+        bool have_prev = false;
+        while (!dead && next_seg(sg)) {
+            const TItem it = decode<PH>(a, r, cur, sg.i);
+            if (it.key != key) {
+                // new token set: E4M3 rows of all K steps, swizzled, and their scales
+                if (nb > 0 && !wwait(B.b_free, (nb - 1) & 1)) break;
+                const uint8_t *src0;
+                const uint8_t *sc0;
+                size_t rstride, sstride;
+                if (PH == 2) { src0 = t.xq; sc0 = t.xs; rstride = D; sstride = D / 128; }
+                else if (it.shared) { src0 = t.sq; sc0 = t.sqs; rstride = I; sstride = I / 128; }
+                else { src0 = t.hq; sc0 = t.hqs; rstride = I; sstride = I / 128; }
+                auto tok_row = [&](int n) -> size_t {
+                    if (PH == 2 && !it.shared) return (size_t)__ldg(a.pair_tok + it.tok0 + n);
+                    return (size_t)(it.tok0 + n);
+                };
+                const int nchunk = it.ntok * nst * 8;
+                for (int c0 = tid; c0 < nchunk; c0 += 4 * NWK) {
+                    uint4 v[4];
+                    int dsto[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int c = c0 + k * NWK;
+                        dsto[k] = -1;
+                        if (c < nchunk) {
+                            const int n = c / (nst * 8), rem = c - n * (nst * 8);
+                            const int s = rem >> 3, ch = rem & 7;
+                            v[k] = ldg128(src0 + tok_row(n) * rstride + s * 128 + ch * 16);
+                            dsto[k] = s * BSTEP + (int)tc::sw128_offset(n, ch);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (dsto[k] >= 0) *reinterpret_cast<uint4 *>(Bsm + dsto[k]) = v[k];
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                {
+                    const bool tv = lane < it.ntok;
+                    const uint8_t *sr = tv ? sc0 + tok_row(lane) * sstride : nullptr;
+                    for (int s = 0; s < nst; ++s) {
+                        const uint32_t w = tv ? 0x01010101u * (uint32_t)__ldg(sr + s) : 0x7f7f7f7fu;
+                        tc::tmem_st4(tm + lane_base + COL_SFB + (uint32_t)(4 * s), w, 0x7f7f7f7fu, 0x7f7f7f7fu,
+                                     0x7f7f7f7fu);
+                    }
+                }
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(B.b_ready);
+                ++nb;
+                key = it.key;
+            }
+            // weight scale factors, GRP K steps at a time
+            for (int g0 = sg.j0; g0 < sg.j1 && !dead; g0 += GRP) {
+                const int g1 = min(g0 + GRP, sg.j1);
+                if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) break;
+                tc::fence_after_sync();
+                const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
+                if (it.shared) {
+                    const uint8_t *s8 = (const uint8_t *)(PH == 2 ? a.ss13 : a.ss2);
+                    const int kb = K / 128;
+                    for (int j = g0; j < g1; ++j) {
+#pragma unroll
+                        for (int tt = 0; tt < 2; ++tt) {
+                            const int rb = PH == 2 ? tt * (I / 128) + it.blk : 2 * it.blk + tt;
+                            const uint32_t w = 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + j);
+                            tc::tmem_st4(cbase + (uint32_t)(((j - g0) * 2 + tt) * 4), w, w, w, w);
+                        }
+                    }
+                } else {
+                    const int ks = K / 32;
+                    const uint8_t *sb = PH == 2 ? a.w13_s + (size_t)it.el * (2 * I) * ks
+                                                : a.w2_s + (size_t)it.el * D * ks;
+                    uint32_t w[GRP][2][4];
+#pragma unroll
+                    for (int jj = 0; jj < GRP; ++jj)
+#pragma unroll
+                        for (int tt = 0; tt < 2; ++tt)
+#pragma unroll
+                            for (int r1 = 0; r1 < 4; ++r1) {
+                                w[jj][tt][r1] = 0x7f7f7f7fu;
+                                if (g0 + jj < g1) {
+                                    const int rr = 32 * r1 + lane;
+                                    const int grow = PH == 2 ? tt * I + it.blk * 128 + rr : it.blk * 256 + tt * 128 + rr;
+                                    w[jj][tt][r1] = __ldg(reinterpret_cast<const uint32_t *>(
+                                        sb + (size_t)grow * ks + (size_t)(g0 + jj) * 4));
+                                }
+                            }
+#pragma unroll
+                    for (int jj = 0; jj < GRP; ++jj)
+                        if (g0 + jj < g1) {
+#pragma unroll
+                            for (int tt = 0; tt < 2; ++tt)
+                                tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
+                                             w[jj][tt][2], w[jj][tt][3]);
+                        }
+                }
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(B.sfa_ready + (gi & 1));
+                ++gi;
+                if (g0 == sg.j0 && have_prev) epilogue(prev);
+            }
+            if (dead) break;
+            prev = sg;
+            have_prev = true;
+        }
+        if (have_prev && !dead) epilogue(prev);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == W_PROD) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tm, 512);
+    }
+}
+
+}  // namespace mtc
