@@ -61,7 +61,10 @@ constexpr int MAX_T = 256;
 constexpr int MAX_PAIRS = MAX_T * MAX_K;
 // routing tables copied to shared memory at kernel start (K2, K3)
 constexpr int OFF_ROUTE = OFF_MISC + MISC_BYTES;
-constexpr int ROUTE_BYTES = 3 * (MAX_E + 1) * 4 + MAX_PAIRS * 2 + MAX_PAIRS * 4;
+constexpr int ROUTE_TABLE_BYTES = 3 * (MAX_E + 1) * 4 + MAX_PAIRS * 2 + MAX_PAIRS * 4;
+// the router CTA's top-k uses the same region: token bitmaps, pair offsets, scan scratch
+constexpr int TOPK_ROUTE_BYTES = MAX_E * (MAX_T / 32) * 4 + MAX_E * 4 + NCW * 8;
+constexpr int ROUTE_BYTES = ROUTE_TABLE_BYTES > TOPK_ROUTE_BYTES ? ROUTE_TABLE_BYTES : TOPK_ROUTE_BYTES;
 constexpr int SMEM_BYTES = OFF_ROUTE + ROUTE_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
@@ -674,52 +677,71 @@ __device__ __forceinline__ float red_sum(const float *red, int arow, int tok) {
 // router (K1, consumer warps): logits[t][e] = sum_k x[t][k] w[e][k] in fp64
 // ---------------------------------------------------------------------------
 __device__ void router_logits(const MoeArgs &a, const Smem &sm) {
+    constexpr int RTP = 4;  // tokens per pass
+    constexpr int KU = 4;   // 256-element chunks of a lane per quarter row (D <= 4096)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = a.E, D = a.D, T = a.T;
     const int G = gridDim.x;
-    static_assert(2 * 4 * TPI * 8 <= MISC_BYTES, "router partials must fit the misc buffer");
-    double *part = sm.misc();  // [2 rows][4 parts][TPI tokens]
+    static_assert(2 * 4 * RTP * 8 <= MISC_BYTES, "router partials must fit the misc buffer");
+    double *part = sm.misc();  // [2 rows][4 parts][RTP tokens]
     const int nrows = (blockIdx.x < E) ? cdiv(E - blockIdx.x, G) : 0;
     const int quarter = D / 4;
     for (int p = 0; p < nrows; p += 2) {
-        for (int t0 = 0; t0 < T; t0 += TPI) {
-            const int rl = warp >> 2, pq = warp & 3;
-            const int r = p + rl;
-            const bool rv = r < nrows;
-            const int e = blockIdx.x + r * G;
-            double accd[TPI];
+        const int rl = warp >> 2, pq = warp & 3;
+        const int r = p + rl;
+        const bool rv = r < nrows;
+        const int e = blockIdx.x + r * G;
+        const __nv_bfloat16 *wrow = a.gate_w + (size_t)(rv ? e : 0) * D + pq * quarter;
+        // every load of a pass is issued before the first use: one memory
+        // latency per pass (the kernel's critical path is latency, not bytes)
+        float wf[KU][8];
+        {
+            uint4 wu[KU];
 #pragma unroll
-            for (int t = 0; t < TPI; ++t) accd[t] = 0.0;
-            if (rv) {
-                const __nv_bfloat16 *wrow = a.gate_w + (size_t)e * D + pq * quarter;
-                for (int k = lane * 8; k < quarter; k += 256) {
-                    const uint4 wu = ldg128(wrow + k);
-                    const uint32_t wv[4] = {wu.x, wu.y, wu.z, wu.w};
-                    float wf[8];
+            for (int u = 0; u < KU; ++u) {
+                const int k = lane * 8 + u * 256;
+                wu[u] = (rv && k < quarter) ? ldg128(wrow + k) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < KU; ++u) {
+                const uint32_t wv[4] = {wu[u].x, wu[u].y, wu[u].z, wu[u].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    wf[u][2 * c] = bf16_bits_to_f32(wv[c] & 0xffffu);
+                    wf[u][2 * c + 1] = bf16_bits_to_f32(wv[c] >> 16);
+                }
+            }
+        }
+        for (int t0 = 0; t0 < T; t0 += RTP) {
+            uint4 xu[KU][RTP];
+#pragma unroll
+            for (int u = 0; u < KU; ++u)
+#pragma unroll
+                for (int t = 0; t < RTP; ++t) {
+                    const int k = lane * 8 + u * 256;
+                    xu[u][t] = (rv && k < quarter && t0 + t < T)
+                                   ? ldg128(a.x + (size_t)(t0 + t) * D + pq * quarter + k)
+                                   : make_uint4(0, 0, 0, 0);
+                }
+            double accd[RTP];
+#pragma unroll
+            for (int t = 0; t < RTP; ++t) {
+                accd[t] = 0.0;
+#pragma unroll
+                for (int u = 0; u < KU; ++u) {
+                    const uint32_t xv[4] = {xu[u][t].x, xu[u][t].y, xu[u][t].z, xu[u][t].w};
+                    double s = 0.0;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        wf[2 * c] = bf16_bits_to_f32(wv[c] & 0xffffu);
-                        wf[2 * c + 1] = bf16_bits_to_f32(wv[c] >> 16);
+                        // bf16 x bf16 products are exact in fp32
+                        s += (double)(wf[u][2 * c] * bf16_bits_to_f32(xv[c] & 0xffffu));
+                        s += (double)(wf[u][2 * c + 1] * bf16_bits_to_f32(xv[c] >> 16));
                     }
-#pragma unroll
-                    for (int t = 0; t < TPI; ++t) {
-                        if (t0 + t < T) {
-                            const uint4 xu = ldg128(a.x + (size_t)(t0 + t) * D + pq * quarter + k);
-                            const uint32_t xv[4] = {xu.x, xu.y, xu.z, xu.w};
-                            double s = 0.0;
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) {
-                                // bf16 x bf16 products are exact in fp32
-                                s += (double)(wf[2 * c] * bf16_bits_to_f32(xv[c] & 0xffffu));
-                                s += (double)(wf[2 * c + 1] * bf16_bits_to_f32(xv[c] >> 16));
-                            }
-                            accd[t] += s;
-                        }
-                    }
+                    accd[t] += s;
                 }
             }
 #pragma unroll
-            for (int t = 0; t < TPI; ++t) {
+            for (int t = 0; t < RTP; ++t) {
                 double v = accd[t];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -727,15 +749,15 @@ __device__ void router_logits(const MoeArgs &a, const Smem &sm) {
             }
             if (lane == 0) {
 #pragma unroll
-                for (int t = 0; t < TPI; ++t) part[(rl * 4 + pq) * TPI + t] = accd[t];
+                for (int t = 0; t < RTP; ++t) part[(rl * 4 + pq) * RTP + t] = accd[t];
             }
             bar_sync(1, NCT);
-            if (threadIdx.x < 2 * TPI) {
-                const int rl2 = threadIdx.x / TPI, t = threadIdx.x % TPI;
+            if (threadIdx.x < 2 * RTP) {
+                const int rl2 = threadIdx.x / RTP, t = threadIdx.x % RTP;
                 const int r2 = p + rl2;
                 if (r2 < nrows && t0 + t < T) {
-                    const double v = part[(rl2 * 4 + 0) * TPI + t] + part[(rl2 * 4 + 1) * TPI + t] +
-                                     part[(rl2 * 4 + 2) * TPI + t] + part[(rl2 * 4 + 3) * TPI + t];
+                    const double v = part[(rl2 * 4 + 0) * RTP + t] + part[(rl2 * 4 + 1) * RTP + t] +
+                                     part[(rl2 * 4 + 2) * RTP + t] + part[(rl2 * 4 + 3) * RTP + t];
                     a.logits[(size_t)(t0 + t) * E + blockIdx.x + r2 * G] = (float)v;
                 }
             }
@@ -753,169 +775,239 @@ __device__ __forceinline__ void warp_argmax(float &v, int &idx) {
     }
 }
 
-// Top-k and dispatch tables; run by the 256 consumer threads of one CTA.
-__device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int T = a.T, E = a.E, K = a.topk;
-    static_assert(2 * MAX_T * MAX_K * 2 <= RED_BYTES, "top-k tables must fit the reduction buffer");
-    static_assert(MAX_E * 4 <= MISC_BYTES, "expert counts must fit the misc buffer");
-    int16_t *ridx_s = reinterpret_cast<int16_t *>(sm.red());          // [T*K]
-    int16_t *pof_s = ridx_s + MAX_T * MAX_K;                            // [T*K]
-    int *cnt_s = reinterpret_cast<int *>(sm.misc());                    // [El]
-    for (int t = warp; t < T; t += NCW) {
-        float sc[MAX_E / 32], bs[MAX_E / 32];
+// Inclusive block scan (NCT threads) of a 64-bit value whose 16-bit fields add
+// independently; `tot` receives the block total.  `ws` holds NCW words.
+__device__ __forceinline__ unsigned long long block_scan_u64(unsigned long long v, unsigned long long *ws,
+                                                             unsigned long long &tot) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) ws[warp] = v;
+    bar_sync(1, NCT);
+    unsigned long long before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) {
+        const unsigned long long x = ws[w];
+        if (w < warp) before += x;
+        all += x;
+    }
+    bar_sync(1, NCT);
+    tot = all;
+    return v + before;
+}
+
+// Top-k of token t by one warp (Gate.forward, architecture.py:696-718): scores,
+// + bias for the choice, K rounds of warp argmax (lowest index on ties),
+// weights from the unbiased scores normalized in slot order (non-softmax)
+// times route_scale.  NE experts per lane; rolled loops keep the code small,
+// since it runs once per launch on a cold instruction cache.
+template <int NE>
+__device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float *sc_w, int16_t *ridx_s,
+                                        int16_t *pof_s, float *rw_s) {
+    const int E = a.E, K = a.topk;
+    float sc[NE], bs[NE];
+#pragma unroll
+    for (int i = 0; i < NE; ++i) {
+        const int e = lane + 32 * i;
+        sc[i] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+    }
+    if (a.score_func == WF_SCORE_SOFTMAX) {
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < MAX_E / 32; ++i) {
+        for (int i = 0; i < NE; ++i) mx = fmaxf(mx, sc[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
             const int e = lane + 32 * i;
-            const float l = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
-            sc[i] = l;
-            mx = fmaxf(mx, l);
-        }
-        if (a.score_func == WF_SCORE_SOFTMAX) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < MAX_E / 32; ++i) {
-                const int e = lane + 32 * i;
-                sc[i] = e < E ? expf(sc[i] - mx) : 0.f;
-                sum += sc[i];
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-            for (int i = 0; i < MAX_E / 32; ++i) sc[i] = sc[i] / sum;
-        } else if (a.score_func == WF_SCORE_SIGMOID) {
-#pragma unroll
-            for (int i = 0; i < MAX_E / 32; ++i) sc[i] = 1.0f / (1.0f + expf(-sc[i]));
-        } else {
-#pragma unroll
-            for (int i = 0; i < MAX_E / 32; ++i) {
-                const float l = sc[i];
-                sc[i] = sqrtf(l > 20.f ? l : log1pf(expf(l)));
-            }
+            sc[i] = e < E ? expf(sc[i] - mx) : 0.f;
+            sum += sc[i];
         }
 #pragma unroll
-        for (int i = 0; i < MAX_E / 32; ++i) {
-            const int e = lane + 32 * i;
-            bs[i] = e < E ? (a.gate_b ? sc[i] + __ldg(a.gate_b + e) : sc[i]) : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+        for (int i = 0; i < NE; ++i) sc[i] = sc[i] / sum;
+    } else if (a.score_func == WF_SCORE_SIGMOID) {
+#pragma unroll
+        for (int i = 0; i < NE; ++i) sc[i] = 1.0f / (1.0f + expf(-sc[i]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            const float l = sc[i];
+            sc[i] = sqrtf(l > 20.f ? l : log1pf(expf(l)));
         }
-        int sel[MAX_K];
+    }
+#pragma unroll
+    for (int i = 0; i < NE; ++i) {
+        const int e = lane + 32 * i;
+        bs[i] = e < E ? (a.gate_b ? sc[i] + __ldg(a.gate_b + e) : sc[i]) : -INFINITY;
+        if (e < E) sc_w[e] = sc[i];
+    }
+    long long id = 0;
+    if (a.hash) {
+        id = __ldg(a.ids + t);
+        if (id < 0 || id >= a.vocab) { if (lane == 0) atomicOr(a.err, kErrExpertId); id = 0; }
+    }
+#pragma unroll 1
+    for (int j = 0; j < K; ++j) {
+        int ej;
         if (a.hash) {
-            long long id = __ldg(a.ids + t);
-            if (id < 0 || id >= a.vocab) { if (lane == 0) atomicOr(a.err, kErrExpertId); id = 0; }
-            for (int j = 0; j < K; ++j) {
-                int e = __ldg(a.tid2eid + id * K + j);
-                if (e < 0 || e >= E) { if (lane == 0) atomicOr(a.err, kErrExpertId); e = 0; }
-                sel[j] = e;
-            }
+            ej = __ldg(a.tid2eid + id * K + j);
+            if (ej < 0 || ej >= E) { if (lane == 0) atomicOr(a.err, kErrExpertId); ej = 0; }
         } else {
-            for (int j = 0; j < K; ++j) {
-                float bv = -INFINITY; int bi = 0x7fffffff;
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
 #pragma unroll
-                for (int i = 0; i < MAX_E / 32; ++i) {
-                    const int e = lane + 32 * i;
-                    if (e < E && (bs[i] > bv || (bs[i] == bv && e < bi))) { bv = bs[i]; bi = e; }
-                }
-                warp_argmax(bv, bi);
-                sel[j] = bi;
-#pragma unroll
-                for (int i = 0; i < MAX_E / 32; ++i)
-                    if (lane + 32 * i == bi) bs[i] = -INFINITY;
+            for (int i = 0; i < NE; ++i) {
+                const int e = lane + 32 * i;
+                if (e < E && (bs[i] > bv || (bs[i] == bv && e < bi))) { bv = bs[i]; bi = e; }
             }
-        }
-        float wsel[MAX_K];
-        float wsum = 0.f;
-        for (int j = 0; j < K; ++j) {
-            const int e = sel[j];
-            float v = 0.f;
+            warp_argmax(bv, bi);
+            ej = bi;
 #pragma unroll
-            for (int i = 0; i < MAX_E / 32; ++i)
-                if (i == (e >> 5)) v = sc[i];
-            v = __shfl_sync(0xffffffffu, v, e & 31);
-            wsel[j] = v;
-            wsum += v;
+            for (int i = 0; i < NE; ++i)
+                if (lane + 32 * i == ej) bs[i] = -INFINITY;
         }
-        if (lane == 0) {
-            for (int j = 0; j < K; ++j) {
-                float w = wsel[j];
-                if (a.score_func != WF_SCORE_SOFTMAX) w = w / wsum;
-                w = w * a.route_scale;
-                a.rw[t * K + j] = w;
-                ridx_s[t * K + j] = (int16_t)sel[j];
-                pof_s[t * K + j] = -1;
-                if (a.out_w) a.out_w[(size_t)t * K + j] = w;
-                if (a.out_idx) a.out_idx[(size_t)t * K + j] = sel[j];
-            }
+        if (lane == 0) ridx_s[t * K + j] = (int16_t)ej;
+    }
+    __syncwarp();
+    float wj = 0.f;
+    int ej = 0;
+    if (lane < K) {
+        ej = ridx_s[t * K + lane];
+        wj = sc_w[ej];
+    }
+    float wsum = 0.f;
+    for (int j = 0; j < K; ++j) wsum += __shfl_sync(0xffffffffu, wj, j);
+    if (lane < K) {
+        float w = wj;
+        if (a.score_func != WF_SCORE_SOFTMAX) w = w / wsum;
+        w = w * a.route_scale;
+        rw_s[t * K + lane] = w;
+        pof_s[t * K + lane] = -1;
+        if (a.out_w) a.out_w[(size_t)t * K + lane] = w;
+        if (a.out_idx) a.out_idx[(size_t)t * K + lane] = ej;
+    }
+    __syncwarp();
+}
+
+// Top-k and dispatch tables; run by the 256 consumer threads of one CTA.
+// Every phase is spread over the block (the router kernel's critical path):
+//   1. top-k per token, one warp per token           -> ridx_s, rw_s, outputs
+//   2. per (token, slot): keep flag (a duplicate keeps its last slot), expert
+//      counts and per-expert token bitmaps (shared-memory atomics)
+//   3. block scan over local experts                 -> act_* tables, header
+//   4. per kept slot: rank among the expert's tokens (bitmap popcount) -> pair
+//   5. per token: its pairs in ascending expert order -> tok_pairs
+__device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int T = a.T, E = a.E, K = a.topk, El = a.El;
+    static_assert(MAX_T * MAX_K * (2 + 2 + 4) <= RED_BYTES, "top-k tables must fit the reduction buffer");
+    static_assert(MAX_E * 4 <= MISC_BYTES, "expert counts must fit the misc buffer");
+    static_assert(TOPK_ROUTE_BYTES <= ROUTE_BYTES, "token bitmaps must fit the route buffer");
+    int16_t *ridx_s = reinterpret_cast<int16_t *>(sm.red());          // [T*K] expert
+    int16_t *pof_s = ridx_s + MAX_T * MAX_K;                            // [T*K] pair or -1
+    float *rw_s = reinterpret_cast<float *>(pof_s + MAX_T * MAX_K);     // [T*K] weight
+    int *cnt_s = reinterpret_cast<int *>(sm.misc());                    // [El]
+    uint32_t *bm = reinterpret_cast<uint32_t *>(sm.base + OFF_ROUTE);   // [El][TW]
+    int *off_s = reinterpret_cast<int *>(bm + MAX_E * (MAX_T / 32));    // [El]
+    unsigned long long *scan_ws = reinterpret_cast<unsigned long long *>(off_s + MAX_E);   // [NCW]
+    const int TW = (T + 31) >> 5;
+    // ---- 1. top-k: one warp per token, scores of the warp's token in shared memory
+    float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);  // [NCW][MAX_E]
+    for (int t = warp; t < T; t += NCW) {
+        if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s);
+        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s);
+    }
+    bar_sync(1, NCT);
+    if (a.route_only) {
+        __threadfence();
+        return;
+    }
+    for (int i = tid; i < El; i += NCT) cnt_s[i] = 0;
+    for (int i = tid; i < El * TW; i += NCT) bm[i] = 0u;
+    bar_sync(1, NCT);
+    // ---- 2. keep flags, counts, bitmaps
+    for (int slot = tid; slot < T * K; slot += NCT) {
+        const int t = slot / K, j = slot - t * K;
+        const int e = ridx_s[slot];
+        bool later = false;
+        for (int j2 = j + 1; j2 < K; ++j2) later |= ridx_s[t * K + j2] == e;
+        const int el = e - a.e0;
+        if (!later && el >= 0 && el < El) {
+            pof_s[slot] = -2;
+            atomicAdd(cnt_s + el, 1);
+            atomicOr(bm + el * TW + (t >> 5), 1u << (t & 31));
         }
     }
-    __threadfence();
     bar_sync(1, NCT);
-    if (a.route_only) return;
-    // per local expert: number of tokens that keep it (a duplicate keeps its last slot)
-    for (int el = tid; el < a.El; el += NCT) {
-        const int e = a.e0 + el;
-        int c = 0;
-        for (int t = 0; t < T; ++t)
-            for (int j = 0; j < K; ++j) {
-                if (ridx_s[t * K + j] != e) continue;
-                bool later = false;
-                for (int j2 = j + 1; j2 < K; ++j2) later |= ridx_s[t * K + j2] == e;
-                c += !later;
-            }
-        cnt_s[el] = c;
-    }
-    bar_sync(1, NCT);
-    if (tid == 0) {
-        int n = 0, off = 0, it2 = 0, it3 = 0, tgt = 0;
-        const int per2 = a.I / a.g.nh13, per3 = a.D / a.g.r2;
-        for (int el = 0; el < a.El; ++el) {
-            const int c = cnt_s[el];
-            if (c) {
-                const int TG = cdiv(c, TPI);
-                a.act_expert[n] = a.e0 + el; a.act_off[n] = off;
-                a.act_it2[n] = it2; a.act_it3[n] = it3;
-                it2 += per2 * TG; it3 += per3 * TG; tgt += TG; off += c;
-                cnt_s[el] = n++;
-            } else {
-                cnt_s[el] = -1;
-            }
+    // ---- 3. scan over local experts (two per thread): pair offset, item offsets, active index
+    const int per2 = a.I / a.g.nh13, per3 = a.D / a.g.r2;
+    int c0 = 0, c1 = 0;
+    const int el0 = 2 * tid, el1 = 2 * tid + 1;
+    if (el0 < El) c0 = cnt_s[el0];
+    if (el1 < El) c1 = cnt_s[el1];
+    auto pack = [](int c) -> unsigned long long {
+        return (unsigned long long)c | ((unsigned long long)cdiv(c, TPI) << 16) |
+               ((unsigned long long)(c > 0) << 32);
+    };
+    const unsigned long long v0 = pack(c0), v1 = pack(c1);
+    unsigned long long tot;
+    const unsigned long long inc = block_scan_u64(v0 + v1, scan_ws, tot);
+    unsigned long long ex0 = inc - v0 - v1;
+    auto emit = [&](int el, int c, unsigned long long ex) {
+        if (el >= El) return;
+        const int off = (int)(ex & 0xffff), tg = (int)((ex >> 16) & 0xffff), n = (int)((ex >> 32) & 0xffff);
+        off_s[el] = off;
+        if (c) {
+            a.act_expert[n] = a.e0 + el;
+            a.act_off[n] = off;
+            a.act_it2[n] = per2 * tg;
+            a.act_it3[n] = per3 * tg;
         }
-        a.act_off[n] = off; a.act_it2[n] = it2; a.act_it3[n] = it3;
-        a.hdr[H_NACT] = n; a.hdr[H_IT2] = it2; a.hdr[H_IT3] = it3; a.hdr[H_TGT] = tgt;
+    };
+    emit(el0, c0, ex0);
+    emit(el1, c1, ex0 + v0);
+    if (tid == NCT - 1) {
+        const int off = (int)(tot & 0xffff), tg = (int)((tot >> 16) & 0xffff), n = (int)((tot >> 32) & 0xffff);
+        a.act_off[n] = off; a.act_it2[n] = per2 * tg; a.act_it3[n] = per3 * tg;
+        a.hdr[H_NACT] = n; a.hdr[H_IT2] = per2 * tg; a.hdr[H_IT3] = per3 * tg; a.hdr[H_TGT] = tg;
         a.hdr[H_NPAIR] = off;
     }
     bar_sync(1, NCT);
-    for (int el = tid; el < a.El; el += NCT) {
-        const int ai = cnt_s[el];
-        if (ai < 0) continue;
-        const int e = a.e0 + el;
-        int p = a.act_off[ai];
-        for (int t = 0; t < T; ++t)
-            for (int j = 0; j < K; ++j) {
-                if (ridx_s[t * K + j] != e) continue;
-                bool later = false;
-                for (int j2 = j + 1; j2 < K; ++j2) later |= ridx_s[t * K + j2] == e;
-                if (later) continue;
-                a.pair_tok[p] = t;
-                a.pair_w[p] = __ldcg(a.rw + t * K + j);
-                pof_s[t * K + j] = (int16_t)p;
-                ++p;
-            }
+    // ---- 4. pairs: expert ascending, token ascending within an expert
+    for (int slot = tid; slot < T * K; slot += NCT) {
+        if (pof_s[slot] != -2) continue;
+        const int t = slot / K;
+        const int el = ridx_s[slot] - a.e0;
+        const uint32_t *row = bm + el * TW;
+        int rank = __popc(row[t >> 5] & ((1u << (t & 31)) - 1u));
+        for (int w = 0; w < (t >> 5); ++w) rank += __popc(row[w]);
+        const int p = off_s[el] + rank;
+        a.pair_tok[p] = t;
+        a.pair_w[p] = rw_s[slot];
+        pof_s[slot] = (int16_t)p;
     }
     bar_sync(1, NCT);
+    // ---- 5. each token's pairs in ascending expert order (a token's kept experts
+    // are distinct, so a slot's place is the number of its kept slots with a
+    // smaller expert)
     for (int t = tid; t < T; t += NCT) {
-        int ee[MAX_K], pp[MAX_K], n = 0;
+        int n = 0;
         for (int j = 0; j < K; ++j) {
             const int p = pof_s[t * K + j];
             if (p < 0) continue;
             const int e = ridx_s[t * K + j];
-            int m = n++;
-            while (m > 0 && ee[m - 1] > e) { ee[m] = ee[m - 1]; pp[m] = pp[m - 1]; --m; }
-            ee[m] = e; pp[m] = p;
+            int rank = 0;
+            for (int j2 = 0; j2 < K; ++j2)
+                rank += (pof_s[t * K + j2] >= 0 && ridx_s[t * K + j2] < e) ? 1 : 0;
+            a.tok_pairs[t * K + rank] = p;
+            ++n;
         }
-        for (int m = 0; m < n; ++m) a.tok_pairs[t * K + m] = pp[m];
         a.tok_np[t] = n;
     }
     __threadfence();
@@ -942,6 +1034,47 @@ __device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
         } else {
             acc += bf16_bits_to_f32(__ldcg(os + (size_t)t * D + r));
             a.y[(size_t)t * D + r] = __float2bfloat16_rn(acc);
+        }
+    }
+}
+
+// combine_rows with 8 consecutive rows of one token per thread (16-byte loads
+// and stores); same fp32 sum in the same order.  nrows and row0 multiples of 8.
+template <int NTH>
+__device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows) {
+    const int T = a.T, D = a.D, K = a.topk, nv = nrows / 8;
+    for (int idx = threadIdx.x; idx < T * nv; idx += NTH) {
+        const int t = idx / nv, r = row0 + 8 * (idx - t * nv);
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+        const int np = __ldcg(a.tok_np + t);
+        for (int qq = 0; qq < np; ++qq) {
+            const int p = __ldcg(a.tok_pairs + t * K + qq);
+            const uint4 v = ldcg128(a.o + (size_t)p * D + r);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                acc[2 * e] += bf16_bits_to_f32(u[e] & 0xffffu);
+                acc[2 * e + 1] += bf16_bits_to_f32(u[e] >> 16);
+            }
+        }
+        if (a.partial) {
+            float4 *dst = reinterpret_cast<float4 *>(a.y_partial + (size_t)t * D + r);
+            dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        } else {
+            const uint4 sv = ldcg128(a.os + (size_t)t * D + r);
+            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float lo = acc[2 * e] + bf16_bits_to_f32(u[e] & 0xffffu);
+                const float hi = acc[2 * e + 1] + bf16_bits_to_f32(u[e] >> 16);
+                o[e] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+                       ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+            }
+            *reinterpret_cast<uint4 *>(a.y + (size_t)t * D + r) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
 }
@@ -987,19 +1120,30 @@ __device__ void quantize_tokens(const MoeArgs &a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = a.D / 128;
     for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-        for (int b = warp; b < nb; b += NCW) {
-            const uint2 u = __ldg(reinterpret_cast<const uint2 *>(a.x + (size_t)t * a.D + b * 128 + 4 * lane));
-            const float v0 = bf16_bits_to_f32(u.x & 0xffffu), v1 = bf16_bits_to_f32(u.x >> 16);
-            const float v2 = bf16_bits_to_f32(u.y & 0xffffu), v3 = bf16_bits_to_f32(u.y >> 16);
-            float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+        for (int b0 = warp; b0 < nb; b0 += 4 * NCW) {
+            uint2 u[4];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float s = round_scale_e8(fmaxf(m, 1e-4f), 1);
-            const float inv = 1.0f / s;  // exact: s is a power of two
-            auto q = [&](float v) { return fminf(fmaxf(v * inv, -448.f), 448.f); };
-            const uint32_t lo = f32x2_to_e4m3x2(q(v0), q(v1)), hi = f32x2_to_e4m3x2(q(v2), q(v3));
-            *reinterpret_cast<uint32_t *>(a.xq + (size_t)t * a.D + b * 128 + 4 * lane) = lo | (hi << 16);
-            if (lane == 0) a.xs[(size_t)t * nb + b] = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
+            for (int q = 0; q < 4; ++q) {
+                const int b = b0 + q * NCW;
+                u[q] = b < nb ? __ldg(reinterpret_cast<const uint2 *>(a.x + (size_t)t * a.D + b * 128 + 4 * lane))
+                              : make_uint2(0, 0);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int b = b0 + q * NCW;
+                if (b >= nb) continue;
+                const float v0 = bf16_bits_to_f32(u[q].x & 0xffffu), v1 = bf16_bits_to_f32(u[q].x >> 16);
+                const float v2 = bf16_bits_to_f32(u[q].y & 0xffffu), v3 = bf16_bits_to_f32(u[q].y >> 16);
+                float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float s = round_scale_e8(fmaxf(m, 1e-4f), 1);
+                const float inv = 1.0f / s;  // exact: s is a power of two
+                auto qz = [&](float v) { return fminf(fmaxf(v * inv, -448.f), 448.f); };
+                const uint32_t lo = f32x2_to_e4m3x2(qz(v0), qz(v1)), hi = f32x2_to_e4m3x2(qz(v2), qz(v3));
+                *reinterpret_cast<uint32_t *>(a.xq + (size_t)t * a.D + b * 128 + 4 * lane) = lo | (hi << 16);
+                if (lane == 0) a.xs[(size_t)t * nb + b] = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
+            }
         }
     }
 }

@@ -298,12 +298,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 bool first = true;
                 bool ok = true;
                 for (int j = sg.j0; j < sg.j1; ++j, ++gs) {
-                    const int jj = j - sg.j0;
-                    const int gj = jj & (GRP - 1);
-                    if (gj == 0) {
+                    // weight-scale groups: K steps [8k, 8k+8) of the item, cut to the segment
+                    const int gj = j & (GRP - 1);
+                    if (j == sg.j0 || gj == 0) {
                         if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort)) { ok = false; break; }
                     }
-                    if ((jj & 1) == ii) {
+                    if (((j - sg.j0) & 1) == ii) {
                         const int st = gs & (STAGES - 1);
                         if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
                         tc::fence_after_sync();
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 bar_sync(1, NWK);
                 if (last) {
                     __threadfence();
-                    combine_rows<NWK>(a, it.blk * 256, 256);
+                    combine_rows_v8<NWK>(a, it.blk * 256, 256);
                     if (tid == 0) a.cnt_rb[it.blk] = 0u;
                 }
             }
@@ -548,9 +548,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 ++nb;
                 key = it.key;
             }
-            // weight scale factors, GRP K steps at a time
-            for (int g0 = sg.j0; g0 < sg.j1 && !dead; g0 += GRP) {
-                const int g1 = min(g0 + GRP, sg.j1);
+            // weight scale factors by groups of K steps [8k, 8k+8) cut to the segment;
+            // the previous segment's epilogue runs once two groups are queued
+            int ngrp = 0;
+            for (int g0 = sg.j0; g0 < sg.j1 && !dead;) {
+                const int g1 = min((g0 & ~(GRP - 1)) + GRP, sg.j1);
                 if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) break;
                 tc::fence_after_sync();
                 const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
@@ -562,31 +564,38 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                         for (int tt = 0; tt < 2; ++tt) {
                             const int rb = PH == 2 ? tt * (I / 128) + it.blk : 2 * it.blk + tt;
                             const uint32_t w = 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + j);
-                            tc::tmem_st4(cbase + (uint32_t)(((j - g0) * 2 + tt) * 4), w, w, w, w);
+                            tc::tmem_st4(cbase + (uint32_t)(((j & (GRP - 1)) * 2 + tt) * 4), w, w, w, w);
                         }
                     }
                 } else {
                     const int ks = K / 32;
                     const uint8_t *sb = PH == 2 ? a.w13_s + (size_t)it.el * (2 * I) * ks
                                                 : a.w2_s + (size_t)it.el * D * ks;
+                    const int ga = g0 & ~(GRP - 1);  // first step of the aligned group
                     uint32_t w[GRP][2][4];
 #pragma unroll
-                    for (int jj = 0; jj < GRP; ++jj)
+                    for (int tt = 0; tt < 2; ++tt)
 #pragma unroll
-                        for (int tt = 0; tt < 2; ++tt)
+                        for (int r1 = 0; r1 < 4; ++r1) {
+                            const int rr = 32 * r1 + lane;
+                            const int grow = PH == 2 ? tt * I + it.blk * 128 + rr : it.blk * 256 + tt * 128 + rr;
+                            const uint8_t *src = sb + (size_t)grow * ks + (size_t)ga * 4;
+                            if ((nst & (GRP - 1)) == 0) {
+                                // the row's 8 words of this group: two 16-byte loads
+                                const uint4 lo = ldg128(src), hi = ldg128(src + 16);
+                                w[0][tt][r1] = lo.x; w[1][tt][r1] = lo.y; w[2][tt][r1] = lo.z; w[3][tt][r1] = lo.w;
+                                w[4][tt][r1] = hi.x; w[5][tt][r1] = hi.y; w[6][tt][r1] = hi.z; w[7][tt][r1] = hi.w;
+                            } else {
 #pragma unroll
-                            for (int r1 = 0; r1 < 4; ++r1) {
-                                w[jj][tt][r1] = 0x7f7f7f7fu;
-                                if (g0 + jj < g1) {
-                                    const int rr = 32 * r1 + lane;
-                                    const int grow = PH == 2 ? tt * I + it.blk * 128 + rr : it.blk * 256 + tt * 128 + rr;
-                                    w[jj][tt][r1] = __ldg(reinterpret_cast<const uint32_t *>(
-                                        sb + (size_t)grow * ks + (size_t)(g0 + jj) * 4));
-                                }
+                                for (int jj = 0; jj < GRP; ++jj)
+                                    w[jj][tt][r1] = (ga + jj >= g0 && ga + jj < g1)
+                                                        ? __ldg(reinterpret_cast<const uint32_t *>(src) + jj)
+                                                        : 0x7f7f7f7fu;
                             }
+                        }
 #pragma unroll
                     for (int jj = 0; jj < GRP; ++jj)
-                        if (g0 + jj < g1) {
+                        if (ga + jj >= g0 && ga + jj < g1) {
 #pragma unroll
                             for (int tt = 0; tt < 2; ++tt)
                                 tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
@@ -598,7 +607,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 __syncwarp();
                 if (lane == 0) mbar_arrive(B.sfa_ready + (gi & 1));
                 ++gi;
-                if (g0 == sg.j0 && have_prev) epilogue(prev);
+                ++ngrp;
+                g0 = g1;
+                if (have_prev && (ngrp == 2 || (ngrp == 1 && g1 == sg.j1))) epilogue(prev);
             }
             if (dead) break;
             prev = sg;
