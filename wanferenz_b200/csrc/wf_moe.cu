@@ -1038,43 +1038,68 @@ __device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
     }
 }
 
-// combine_rows with 8 consecutive rows of one token per thread (16-byte loads
-// and stores); same fp32 sum in the same order.  nrows and row0 multiples of 8.
+// combine_rows with 8 consecutive rows of one token per item (16-byte loads and
+// stores) and two items per thread whose pair lists and pair rows are all
+// loaded before the first add; same fp32 sum in the same order.  nrows and
+// row0 are multiples of 8.
 template <int NTH>
 __device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows) {
-    const int T = a.T, D = a.D, K = a.topk, nv = nrows / 8;
-    for (int idx = threadIdx.x; idx < T * nv; idx += NTH) {
-        const int t = idx / nv, r = row0 + 8 * (idx - t * nv);
-        float acc[8];
+    const int T = a.T, D = a.D, K = a.topk, nv = nrows / 8, n = T * nv;
+    for (int base = threadIdx.x; base < n; base += 2 * NTH) {
+        int tt[2], rr[2], np[2], pr[2][MAX_K];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-        const int np = __ldcg(a.tok_np + t);
-        for (int qq = 0; qq < np; ++qq) {
-            const int p = __ldcg(a.tok_pairs + t * K + qq);
-            const uint4 v = ldcg128(a.o + (size_t)p * D + r);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 2; ++j) {
+            const int idx = base + j * NTH;
+            const bool ok = idx < n;
+            tt[j] = ok ? idx / nv : 0;
+            rr[j] = row0 + 8 * (ok ? idx - tt[j] * nv : 0);
+            np[j] = ok ? __ldcg(a.tok_np + tt[j]) : 0;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                acc[2 * e] += bf16_bits_to_f32(u[e] & 0xffffu);
-                acc[2 * e + 1] += bf16_bits_to_f32(u[e] >> 16);
-            }
+            for (int q = 0; q < MAX_K; ++q) pr[j][q] = (ok && q < K) ? __ldcg(a.tok_pairs + tt[j] * K + q) : 0;
         }
-        if (a.partial) {
-            float4 *dst = reinterpret_cast<float4 *>(a.y_partial + (size_t)t * D + r);
-            dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-        } else {
-            const uint4 sv = ldcg128(a.os + (size_t)t * D + r);
-            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
-            uint32_t o[4];
+        uint4 v[2][MAX_K];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float lo = acc[2 * e] + bf16_bits_to_f32(u[e] & 0xffffu);
-                const float hi = acc[2 * e + 1] + bf16_bits_to_f32(u[e] >> 16);
-                o[e] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
-                       ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int q = 0; q < MAX_K; ++q)
+                v[j][q] = q < np[j] ? ldcg128(a.o + (size_t)pr[j][q] * D + rr[j]) : make_uint4(0, 0, 0, 0);
+        uint4 sv[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+            sv[j] = (!a.partial && base + j * NTH < n) ? ldcg128(a.os + (size_t)tt[j] * D + rr[j]) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            if (base + j * NTH >= n) continue;
+            float acc[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+            for (int q = 0; q < MAX_K; ++q) {
+                if (q >= np[j]) break;
+                const uint32_t u[4] = {v[j][q].x, v[j][q].y, v[j][q].z, v[j][q].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    acc[2 * e] += bf16_bits_to_f32(u[e] & 0xffffu);
+                    acc[2 * e + 1] += bf16_bits_to_f32(u[e] >> 16);
+                }
             }
-            *reinterpret_cast<uint4 *>(a.y + (size_t)t * D + r) = make_uint4(o[0], o[1], o[2], o[3]);
+            const int t = tt[j], r = rr[j];
+            if (a.partial) {
+                float4 *dst = reinterpret_cast<float4 *>(a.y_partial + (size_t)t * D + r);
+                dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+            } else {
+                const uint32_t u[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float lo = acc[2 * e] + bf16_bits_to_f32(u[e] & 0xffffu);
+                    const float hi = acc[2 * e + 1] + bf16_bits_to_f32(u[e] >> 16);
+                    o[e] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+                           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+                }
+                *reinterpret_cast<uint4 *>(a.y + (size_t)t * D + r) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
         }
     }
 }

@@ -23,20 +23,20 @@
 // byte per element (FP4 E2M1 is unpacked by TMA type 16U4_ALIGN16B, FP8 E4M3
 // is copied as is), 128-byte swizzle, as two M = 128 tiles.
 //
-// Warp roles (224 threads):
+// Warp roles (256 threads):
 //   warps 0-3  workers: B operand (the item's tokens as E4M3, all K steps) in
 //              shared memory, B scales and weight scales in TMEM, epilogue
 //              (TMEM -> registers, SwiGLU + quantization or bf16 output)
 //   warp 4     TMA producer of the weight stages
-//   warps 5-6  MMA issuers: issuer i issues the steps of local parity i of a
-//              segment into its own accumulators (one thread issuing block-
-//              scaled MMAs back to back is the throughput limit, two are not)
+//   warps 5-7  MMA issuers: issuer i issues steps i, i+3, i+6, ... of a segment
+//              into its own accumulators (one thread issues a block-scaled MMA
+//              in ~150 cycles; three keep up with HBM)
 #pragma once
 
 namespace mtc {
 
-constexpr int W_PROD = 4, W_ISS0 = 5, NISS = 2;
-constexpr int THREADS = 7 * 32;
+constexpr int W_PROD = 4, W_ISS0 = 5, NISS = 3;
+constexpr int THREADS = 8 * 32;
 constexpr int NWK = 128;                 // worker threads
 constexpr int STAGES = 4;
 constexpr int STAGE_BYTES = 32768;
@@ -48,17 +48,20 @@ constexpr int GRP = 8;                   // K steps per weight-scale group
 constexpr int OFF_A = 0;
 constexpr int OFF_B = STAGES * STAGE_BYTES;
 constexpr int OFF_BAR = OFF_B + MAX_STEPS * BSTEP;
-constexpr int NBAR = 2 * STAGES + 12;
-constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr int OFF_EX = OFF_MISC + 64;            // [4 warps][NT] amax exchange
-constexpr int OFF_ROUTE = OFF_EX + 4 * NT * 4;   // act_expert, act_off, act_it
+constexpr int NBAR = 2 * STAGES + 10 + NISS;  // ..., fin[NISS]
+constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 127) / 128 * 128;
+constexpr int AM_LD = NT + 4;                    // amax tile row: 16-byte aligned, conflict-free reads
+constexpr int OFF_EX = OFF_MISC + 128;           // [128 rows][AM_LD] |h|, then [NT] scales
+constexpr int EX_BYTES = (128 * AM_LD + 2 * NT) * 4;
+constexpr int OFF_ROUTE = OFF_EX + EX_BYTES;     // act_expert, act_off, act_it
 constexpr int ROUTE_BYTES = 3 * (MAX_E + 1) * 4;
 constexpr int SMEM = OFF_ROUTE + ROUTE_BYTES + 1024;  // + alignment slack
 static_assert(SMEM <= 232448, "shared memory budget");
+static_assert(OFF_EX % 16 == 0 && (AM_LD * 4) % 16 == 0, "float4 rows of the amax tile");
 // TMEM columns (512 allocated)
 constexpr uint32_t COL_D = 0;      // [issuer][buf][tile] x NT
-constexpr uint32_t COL_SFB = 128;  // [K step] x 4
-constexpr uint32_t COL_SFA = 256;  // [group buf][step in group][tile] x 4
+constexpr uint32_t COL_SFB = 192;  // [K step] x 4
+constexpr uint32_t COL_SFA = 320;  // [group buf][step in group][tile] x 4
 static_assert(COL_D + NISS * 2 * 2 * NT <= COL_SFB, "accumulator columns");
 static_assert(COL_SFB + MAX_STEPS * 4 <= COL_SFA, "B scale columns");
 static_assert(COL_SFA + 2 * GRP * 2 * 4 <= 512, "weight scale columns");
@@ -90,7 +93,7 @@ __device__ __forceinline__ Bars bars_at(uint8_t *base) {
     r.sfa_free = b + 2 * STAGES + 4;   // [2]
     r.d_ready = b + 2 * STAGES + 6;    // [2]
     r.d_free = b + 2 * STAGES + 8;     // [2]
-    r.fin = b + 2 * STAGES + 10;       // [2] issuer drain
+    r.fin = b + 2 * STAGES + 10;       // [NISS] issuer drain
     return r;
 }
 
@@ -193,8 +196,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         for (int j = 0; j < 2; ++j) {
             mbar_init(B.sfa_ready + j, 4); mbar_init(B.sfa_free + j, NISS);
             mbar_init(B.d_ready + j, NISS); mbar_init(B.d_free + j, 4);
-            mbar_init(B.fin + j, 1);
         }
+        for (int j = 0; j < NISS; ++j) mbar_init(B.fin + j, 1);
         *abort = 0;
         *flag = 0;
         fence_mbar_init();
@@ -297,13 +300,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 const uint32_t dcol = tm + COL_D + (uint32_t)((ii * 2 + buf) * 2 * NT);
                 bool first = true;
                 bool ok = true;
-                for (int j = sg.j0; j < sg.j1; ++j, ++gs) {
+                int own = 0;  // issuer of step j: (j - j0) mod NISS
+                for (int j = sg.j0; j < sg.j1; ++j, ++gs, own = (own + 1 == NISS) ? 0 : own + 1) {
                     // weight-scale groups: K steps [8k, 8k+8) of the item, cut to the segment
                     const int gj = j & (GRP - 1);
                     if (j == sg.j0 || gj == 0) {
                         if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort)) { ok = false; break; }
                     }
-                    if (((j - sg.j0) & 1) == ii) {
+                    if (own == ii) {
                         const int st = gs & (STAGES - 1);
                         if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
                         tc::fence_after_sync();
@@ -363,28 +367,27 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
             const int buf = e.q & 1;
             if (!wwait(B.d_ready + buf, (e.q >> 1) & 1)) return;
             tc::fence_after_sync();
-            uint32_t v0[NT], v1[NT], w0[NT], w1[NT];
-            tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((0 * 2 + buf) * 2 * NT), v0);
-            tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((0 * 2 + buf) * 2 * NT + NT), v1);
-            const bool two = e.j1 - e.j0 >= 2;
-            if (two) {
-                tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((1 * 2 + buf) * 2 * NT), w0);
-                tc::tmem_ld16(tm + lane_base + COL_D + (uint32_t)((1 * 2 + buf) * 2 * NT + NT), w1);
+            // sum of the issuers' accumulators in issuer order (issuer i has steps
+            // iff the segment has more than i)
+            float g[NT], u[NT];
+            const int nsteps = e.j1 - e.j0;
+#pragma unroll
+            for (int ii = 0; ii < NISS; ++ii) {
+                if (ii > 0 && nsteps <= ii) break;
+                uint32_t v0[NT], v1[NT];
+                const uint32_t col = COL_D + (uint32_t)((ii * 2 + buf) * 2 * NT);
+                tc::tmem_ld16(tm + lane_base + col, v0);
+                tc::tmem_ld16(tm + lane_base + col + NT, v1);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    if (ii == 0) { g[n] = __uint_as_float(v0[n]); u[n] = __uint_as_float(v1[n]); }
+                    else { g[n] += __uint_as_float(v0[n]); u[n] += __uint_as_float(v1[n]); }
+                }
             }
-            tc::tmem_wait_ld();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(B.d_free + buf);
-            float g[NT], u[NT];
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                g[n] = __uint_as_float(v0[n]);
-                u[n] = __uint_as_float(v1[n]);
-                if (two) {
-                    g[n] += __uint_as_float(w0[n]);
-                    u[n] += __uint_as_float(w1[n]);
-                }
-            }
             const int ntok = it.ntok;
             if (!(e.j0 == 0 && e.j1 == nst)) {
                 // stream-K: this segment's partial sums go to the CTA's slot; the last
@@ -393,11 +396,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 const int mine = blockIdx.x * 2 + (u0 >= is ? 0 : 1);
                 float *ps = t.part + (size_t)mine * (2 * 128 * NT);
 #pragma unroll
-                for (int n = 0; n < NT; ++n)
+                for (int n = 0; n < NT; ++n) {
+                    if ((n & 3) == 0 && n >= ntok) break;
                     if (n < ntok) {
                         ps[(0 * 128 + row) * NT + n] = g[n];
                         ps[(1 * 128 + row) * NT + n] = u[n];
                     }
+                }
                 __threadfence();
                 bar_sync(1, NWK);
                 if (tid == 0) {
@@ -421,35 +426,51 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     if (cta_start(b + 1, S, G) <= ub) continue;
                     const float *pp = t.part + (size_t)(b * 2 + (ub >= is ? 0 : 1)) * (2 * 128 * NT);
 #pragma unroll
-                    for (int n = 0; n < NT; ++n)
+                    for (int n = 0; n < NT; ++n) {
+                        if ((n & 3) == 0 && n >= ntok) break;
                         if (n < ntok) {
                             g[n] += __ldcg(pp + (0 * 128 + row) * NT + n);
                             u[n] += __ldcg(pp + (1 * 128 + row) * NT + n);
                         }
+                    }
                 }
                 if (tid == 0) t.cnt[e.i] = 0u;
             }
             if (PH == 2) {
-                // SwiGLU (architecture.py:733-741) then act_quant of this 128-row block
+                // SwiGLU (architecture.py:733-741) then act_quant of this 128-row block.
+                // The per-token amax over the 128 rows goes through a shared-memory
+                // transpose: |h| tile [row][token], 8 threads per token reduce it.
                 float h[NT];
-                float am[NT];
 #pragma unroll
-                for (int n = 0; n < NT; ++n) {
-                    float hv = 0.f;
-                    if (n < ntok) {
-                        hv = swiglu(g[n], u[n], a.swiglu_limit);
-                        if (!it.shared) hv = __ldg(a.pair_w + it.tok0 + n) * hv;
-                        hv = bf16r(hv);
+                for (int c = 0; c < NT / 4; ++c) {
+                    if (4 * c >= ntok) break;  // whole chunks of 4 tokens
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int n = 4 * c + k;
+                        float hv = swiglu(g[n], u[n], a.swiglu_limit);
+                        if (!it.shared) hv = (n < ntok ? __ldg(a.pair_w + it.tok0 + n) : 0.f) * hv;
+                        h[n] = n < ntok ? bf16r(hv) : 0.f;
                     }
-                    h[n] = hv;
-                    float m = fabsf(hv);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                    am[n] = m;
+                    *reinterpret_cast<float4 *>(ex + row * AM_LD + 4 * c) =
+                        make_float4(fabsf(h[4 * c]), fabsf(h[4 * c + 1]), fabsf(h[4 * c + 2]), fabsf(h[4 * c + 3]));
                 }
-                if (lane == 0) {
+                bar_sync(1, NWK);
+                float *inv_s = ex + 128 * AM_LD;        // [NT] 1/scale
+                uint32_t *sb_s = reinterpret_cast<uint32_t *>(inv_s + NT);  // [NT] e8m0 byte
+                {
+                    const int n = tid >> 3, part = tid & 7;  // 16 tokens x 8 threads
+                    float m = 0.f;
+                    if (n < ntok) {
 #pragma unroll
-                    for (int n = 0; n < NT; ++n) ex[wq * NT + n] = am[n];
+                        for (int i = 0; i < 16; ++i) m = fmaxf(m, ex[(part + 8 * i) * AM_LD + n]);
+                    }
+#pragma unroll
+                    for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    if (part == 0 && n < ntok) {
+                        const float sc = round_scale_e8(fmaxf(m, 1e-4f), 1);
+                        inv_s[n] = 1.0f / sc;  // exact: sc is a power of two
+                        sb_s[n] = (__float_as_uint(sc) >> 23) & 0xffu;
+                    }
                 }
                 bar_sync(1, NWK);
                 uint8_t *dq = it.shared ? t.sq : t.hq;
@@ -457,21 +478,18 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 const int ib = I / 128;
 #pragma unroll
                 for (int n = 0; n < NT; ++n) {
-                    if (n >= ntok) continue;
-                    const float amax = fmaxf(fmaxf(ex[n], ex[NT + n]), fmaxf(ex[2 * NT + n], ex[3 * NT + n]));
-                    const float s = round_scale_e8(fmaxf(amax, 1e-4f), 1);
-                    const float inv = 1.0f / s;
-                    const float qv = fminf(fmaxf(h[n] * inv, -448.f), 448.f);
+                    if (n >= ntok) break;
+                    const float qv = fminf(fmaxf(h[n] * inv_s[n], -448.f), 448.f);
                     const size_t prow = (size_t)(it.tok0 + n);
                     dq[prow * I + it.blk * 128 + row] = e4m3_byte(qv);
-                    if (tid == 0) ds[prow * ib + it.blk] = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
                 }
-                bar_sync(1, NWK);  // the exchange buffer is reused by the next epilogue
+                if (tid < ntok) ds[(size_t)(it.tok0 + tid) * ib + it.blk] = (uint8_t)sb_s[tid];
+                bar_sync(1, NWK);  // the tile is reused by the next epilogue
             } else {
                 __nv_bfloat16 *dst = it.shared ? a.os : a.o;
 #pragma unroll
                 for (int n = 0; n < NT; ++n) {
-                    if (n >= ntok) continue;
+                    if (n >= ntok) break;
                     const size_t o = (size_t)(it.tok0 + n) * D + it.blk * 256 + row;
                     dst[o] = __float2bfloat16_rn(g[n]);
                     dst[o + 128] = __float2bfloat16_rn(u[n]);
@@ -513,11 +531,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     return (size_t)(it.tok0 + n);
                 };
                 const int nchunk = it.ntok * nst * 8;
-                for (int c0 = tid; c0 < nchunk; c0 += 4 * NWK) {
-                    uint4 v[4];
-                    int dsto[4];
+                for (int c0 = tid; c0 < nchunk; c0 += 8 * NWK) {
+                    uint4 v[8];
+                    int dsto[8];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
+                    for (int k = 0; k < 8; ++k) {
                         const int c = c0 + k * NWK;
                         dsto[k] = -1;
                         if (c < nchunk) {
@@ -528,7 +546,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                         }
                     }
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
+                    for (int k = 0; k < 8; ++k)
                         if (dsto[k] >= 0) *reinterpret_cast<uint4 *>(Bsm + dsto[k]) = v[k];
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -553,26 +571,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
             int ngrp = 0;
             for (int g0 = sg.j0; g0 < sg.j1 && !dead;) {
                 const int g1 = min((g0 & ~(GRP - 1)) + GRP, sg.j1);
-                if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) break;
-                tc::fence_after_sync();
-                const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
+                const int ga = g0 & ~(GRP - 1);  // first step of the aligned group
+                // global loads first; the wait below only guards the TMEM slot
+                uint32_t w[GRP][2][4];
                 if (it.shared) {
                     const uint8_t *s8 = (const uint8_t *)(PH == 2 ? a.ss13 : a.ss2);
                     const int kb = K / 128;
-                    for (int j = g0; j < g1; ++j) {
+#pragma unroll
+                    for (int jj = 0; jj < GRP; ++jj)
 #pragma unroll
                         for (int tt = 0; tt < 2; ++tt) {
                             const int rb = PH == 2 ? tt * (I / 128) + it.blk : 2 * it.blk + tt;
-                            const uint32_t w = 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + j);
-                            tc::tmem_st4(cbase + (uint32_t)(((j & (GRP - 1)) * 2 + tt) * 4), w, w, w, w);
+                            const uint32_t v = (ga + jj >= g0 && ga + jj < g1)
+                                                   ? 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + ga + jj)
+                                                   : 0x7f7f7f7fu;
+                            w[jj][tt][0] = w[jj][tt][1] = w[jj][tt][2] = w[jj][tt][3] = v;
                         }
-                    }
                 } else {
                     const int ks = K / 32;
                     const uint8_t *sb = PH == 2 ? a.w13_s + (size_t)it.el * (2 * I) * ks
                                                 : a.w2_s + (size_t)it.el * D * ks;
-                    const int ga = g0 & ~(GRP - 1);  // first step of the aligned group
-                    uint32_t w[GRP][2][4];
 #pragma unroll
                     for (int tt = 0; tt < 2; ++tt)
 #pragma unroll
@@ -593,15 +611,18 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                                                         : 0x7f7f7f7fu;
                             }
                         }
-#pragma unroll
-                    for (int jj = 0; jj < GRP; ++jj)
-                        if (ga + jj >= g0 && ga + jj < g1) {
-#pragma unroll
-                            for (int tt = 0; tt < 2; ++tt)
-                                tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
-                                             w[jj][tt][2], w[jj][tt][3]);
-                        }
                 }
+                if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) break;
+                tc::fence_after_sync();
+                const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
+#pragma unroll
+                for (int jj = 0; jj < GRP; ++jj)
+                    if (ga + jj >= g0 && ga + jj < g1) {
+#pragma unroll
+                        for (int tt = 0; tt < 2; ++tt)
+                            tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
+                                         w[jj][tt][2], w[jj][tt][3]);
+                    }
                 tc::tmem_wait_st();
                 tc::fence_before_sync();
                 __syncwarp();
