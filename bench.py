@@ -195,6 +195,23 @@ def make_layer(seed, rank, world, max_tokens, device, init="quant", zipf_beta=0.
 # ---------------------------------------------------------------------------
 # algorithmic bytes per kernel for one step, from the step's routing
 # ---------------------------------------------------------------------------
+def tc_engine():
+    """The library runs the expert phases on tcgen05 unless WF_DISABLE_TC is set (this
+    benchmark's layers always have e8m0 scales, the other condition)."""
+    return os.environ.get("WF_DISABLE_TC", "0") in ("", "0")
+
+
+def kernel_names():
+    if tc_engine():
+        return ["k_moe_up", "k_moe_tc<2>", "k_moe_tc<3>"]
+    return ["k_moe_up", "k_moe_mid", "k_moe_down"]
+
+
+# ncu traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the tcgen05
+# expert phases, 16 tokens, uniform routing: profiles/k_moe_tc_config2_T16.md
+MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 759.0e6, "k_moe_tc<3>": 389.6e6}
+
+
 def step_bytes(indices, T, e0, El):
     """Bytes each kernel must move at minimum, given this step's expert indices [T, k]."""
     import numpy as np
@@ -205,10 +222,19 @@ def step_bytes(indices, T, e0, El):
     pairs = sum(len(set(r[(r >= e0) & (r < e0 + El)].tolist())) for r in idx)
     w13 = 2 * I * (D // 2 + D // 32)
     w2 = D * (I // 2 + I // 32)
-    k1 = ROUTER_BYTES + 2 * I * D + 2 * (I // 128) * (D // 128) + T * D * 2 + T * I * 2
-    k2 = n_exp * w13 + D * I + (D // 128) * (I // 128) + T * D * 2 + pairs * I * 2 + T * I * 2 + T * D * 2
-    k3 = n_exp * w2 + pairs * I * 2 + pairs * D * 2 * 2 + T * D * 2 * 2
-    return {"k_moe_up": k1, "k_moe_mid": k2, "k_moe_down": k3, "experts": n_exp, "pairs": pairs}
+    s13 = 2 * I * D + 2 * (I // 128) * (D // 128)
+    s2 = D * I + (D // 128) * (I // 128)
+    n1, n2, n3 = kernel_names()
+    if tc_engine():
+        # router + token quantization | routed + shared w1/w3 -> E4M3 hidden | w2 + combine
+        k1 = ROUTER_BYTES + T * D * 2 + T * D + T * D // 128
+        k2 = n_exp * w13 + s13 + T * D + pairs * I + T * I
+        k3 = n_exp * w2 + s2 + pairs * I + T * I + (pairs + T) * D * 2 * 2 + T * D * 2
+    else:
+        k1 = ROUTER_BYTES + s13 + T * D * 2 + T * I * 2
+        k2 = n_exp * w13 + s2 + T * D * 2 + pairs * I * 2 + T * I * 2 + T * D * 2
+        k3 = n_exp * w2 + pairs * I * 2 + pairs * D * 2 * 2 + T * D * 2 * 2
+    return {n1: k1, n2: k2, n3: k3, "experts": n_exp, "pairs": pairs}
 
 
 # ---------------------------------------------------------------------------
@@ -316,12 +342,12 @@ def run_gpu(args):
             one(i, timed=True)
         torch.cuda.synchronize()
         del big
-        kern = {"k_moe_up": [], "k_moe_mid": [], "k_moe_down": []}
+        names = kernel_names()
+        kern = {k: [] for k in names}
         for i in range(W, n):
             e = evs[i]
-            kern["k_moe_up"].append(e[0].elapsed_time(e[1]))
-            kern["k_moe_mid"].append(e[1].elapsed_time(e[2]))
-            kern["k_moe_down"].append(e[2].elapsed_time(e[3]))
+            for j, k in enumerate(names):
+                kern[k].append(e[j].elapsed_time(e[j + 1]))
         routing = [idx[i].cpu().numpy() for i in range(W, n)]
         del g
         return total_ms, kern, routing, clk.summary()
@@ -337,7 +363,7 @@ def run_gpu(args):
         byts = [step_bytes(r, Tloc * world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
-        layer_bytes = mean["k_moe_up"] + mean["k_moe_mid"] + mean["k_moe_down"]
+        layer_bytes = sum(mean[k] for k in kernel_names())
         hist = [np.bincount(r.ravel(), minlength=E) for r in routing]
         tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
                "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
@@ -365,6 +391,11 @@ def run_gpu(args):
     dom = max(kms, key=kms.get)
     ach = main["bytes"][dom] / (kms[dom] * 1e-3) / 1e9
     value = T * world / (main["ms"] * 1e-3)
+    traffic, traffic_src = None, None
+    if dom in MEASURED_TRAFFIC_T16 and T == 16 and world == 1 and args.routing == "uniform":
+        traffic = MEASURED_TRAFFIC_T16[dom]
+        traffic_src = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload "
+                       "(1 layer, random FP4 bytes): profiles/k_moe_tc_config2_T16.md")
 
     e2e = None
     if not args.no_e2e:
@@ -394,7 +425,8 @@ def run_gpu(args):
         },
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / hbm, 4),
-                     "traffic": None, "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
+                     "traffic": traffic, "traffic_source": traffic_src,
+                     "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
         "clocks": main["clocks"],
         "gpu_launches": 3 * args.steps if world == 1 else 4 * args.steps,
         "e2e": e2e,
