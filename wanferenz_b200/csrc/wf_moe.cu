@@ -676,7 +676,7 @@ __device__ __forceinline__ float red_sum(const float *red, int arow, int tok) {
 // ---------------------------------------------------------------------------
 // router (K1, consumer warps): logits[t][e] = sum_k x[t][k] w[e][k] in fp64
 // ---------------------------------------------------------------------------
-__device__ void router_logits(const MoeArgs &a, const Smem &sm) {
+__device__ void router_logits(const MoeArgs &a, const Smem &sm, const __nv_bfloat16 *xsm) {
     constexpr int RTP = 4;  // tokens per pass
     constexpr int KU = 4;   // 256-element chunks of a lane per quarter row (D <= 4096)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -719,8 +719,9 @@ __device__ void router_logits(const MoeArgs &a, const Smem &sm) {
 #pragma unroll
                 for (int t = 0; t < RTP; ++t) {
                     const int k = lane * 8 + u * 256;
+                    const size_t off = (size_t)(t0 + t) * D + pq * quarter + k;
                     xu[u][t] = (rv && k < quarter && t0 + t < T)
-                                   ? ldg128(a.x + (size_t)(t0 + t) * D + pq * quarter + k)
+                                   ? (xsm ? lds128(xsm + off) : ldg128(a.x + off))
                                    : make_uint4(0, 0, 0, 0);
                 }
             double accd[RTP];
@@ -804,9 +805,12 @@ __device__ __forceinline__ unsigned long long block_scan_u64(unsigned long long 
 // weights from the unbiased scores normalized in slot order (non-softmax)
 // times route_scale.  NE experts per lane; rolled loops keep the code small,
 // since it runs once per launch on a cold instruction cache.
+// dry: a warm-up pass on whatever the logits hold (shared-memory outputs only,
+// no global writes, no error reports) that loads this code into the SM's
+// instruction cache before the real pass runs on the last router CTA.
 template <int NE>
 __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float *sc_w, int16_t *ridx_s,
-                                        int16_t *pof_s, float *rw_s) {
+                                        int16_t *pof_s, float *rw_s, bool dry) {
     const int E = a.E, K = a.topk;
     float sc[NE], bs[NE];
 #pragma unroll
@@ -850,14 +854,14 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
     long long id = 0;
     if (a.hash) {
         id = __ldg(a.ids + t);
-        if (id < 0 || id >= a.vocab) { if (lane == 0) atomicOr(a.err, kErrExpertId); id = 0; }
+        if (id < 0 || id >= a.vocab) { if (lane == 0 && !dry) atomicOr(a.err, kErrExpertId); id = 0; }
     }
 #pragma unroll 1
     for (int j = 0; j < K; ++j) {
         int ej;
         if (a.hash) {
             ej = __ldg(a.tid2eid + id * K + j);
-            if (ej < 0 || ej >= E) { if (lane == 0) atomicOr(a.err, kErrExpertId); ej = 0; }
+            if (ej < 0 || ej >= E) { if (lane == 0 && !dry) atomicOr(a.err, kErrExpertId); ej = 0; }
         } else {
             float bv = -INFINITY;
             int bi = 0x7fffffff;
@@ -867,7 +871,7 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
                 if (e < E && (bs[i] > bv || (bs[i] == bv && e < bi))) { bv = bs[i]; bi = e; }
             }
             warp_argmax(bv, bi);
-            ej = bi;
+            ej = (bi >= 0 && bi < E) ? bi : 0;  // a dry pass may see non-finite scores
 #pragma unroll
             for (int i = 0; i < NE; ++i)
                 if (lane + 32 * i == ej) bs[i] = -INFINITY;
@@ -889,8 +893,8 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
         w = w * a.route_scale;
         rw_s[t * K + lane] = w;
         pof_s[t * K + lane] = -1;
-        if (a.out_w) a.out_w[(size_t)t * K + lane] = w;
-        if (a.out_idx) a.out_idx[(size_t)t * K + lane] = ej;
+        if (!dry && a.out_w) a.out_w[(size_t)t * K + lane] = w;
+        if (!dry && a.out_idx) a.out_idx[(size_t)t * K + lane] = ej;
     }
     __syncwarp();
 }
@@ -920,8 +924,8 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
     // ---- 1. top-k: one warp per token, scores of the warp's token in shared memory
     float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);  // [NCW][MAX_E]
     for (int t = warp; t < T; t += NCW) {
-        if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s);
-        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s);
+        if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
     }
     bar_sync(1, NCT);
     if (a.route_only) {
@@ -1139,24 +1143,25 @@ struct NoPreq {
 };
 
 // act_quant (torch_ops.py:33-49) of the layer input for the tcgen05 expert
-// phases: token t by CTA t mod grid, one 128-block per warp at a time, four
-// elements per lane.  Scales are powers of two (ue8m0), stored as e8m0 bytes.
-__device__ void quantize_tokens(const MoeArgs &a) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// phases, by one warp: token t by CTA t mod grid, eight 128-blocks per round
+// (loads first), four elements per lane.  Scales are powers of two (ue8m0),
+// stored as e8m0 bytes.
+__device__ void quantize_tokens_warp(const MoeArgs &a) {
+    const int lane = threadIdx.x & 31;
     const int nb = a.D / 128;
     for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-        for (int b0 = warp; b0 < nb; b0 += 4 * NCW) {
-            uint2 u[4];
+        for (int b0 = 0; b0 < nb; b0 += 8) {
+            uint2 u[8];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int b = b0 + q * NCW;
+            for (int q = 0; q < 8; ++q) {
+                const int b = b0 + q;
                 u[q] = b < nb ? __ldg(reinterpret_cast<const uint2 *>(a.x + (size_t)t * a.D + b * 128 + 4 * lane))
                               : make_uint2(0, 0);
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int b = b0 + q * NCW;
-                if (b >= nb) continue;
+            for (int q = 0; q < 8; ++q) {
+                const int b = b0 + q;
+                if (b >= nb) break;
                 const float v0 = bf16_bits_to_f32(u[q].x & 0xffffu), v1 = bf16_bits_to_f32(u[q].x >> 16);
                 const float v2 = bf16_bits_to_f32(u[q].y & 0xffffu), v3 = bf16_bits_to_f32(u[q].y >> 16);
                 float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
@@ -1183,12 +1188,36 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0, nullptr, nullptr, nullptr); };
+    // tcgen05 mode: the ring is idle, so up to TPI token rows are staged in it with
+    // one bulk copy for the router, and the producer warp quantizes the tokens
+    const size_t xbytes = (size_t)a.T * a.D * 2;
+    const bool stage_x = a.tc && a.T <= TPI && xbytes + 8192 <= (size_t)NSLOT * SLOT_BYTES &&
+                         blockIdx.x < (unsigned)a.E;
     if ((threadIdx.x >> 5) == NCW) {
+        if (a.tc) {
+            if (stage_x && (threadIdx.x & 31) == 0) {
+                mbar_arrive_expect_tx(sm.full(0), (uint32_t)xbytes);
+                bulk_g2s(sm.slot(0), a.x, (uint32_t)xbytes, sm.full(0));
+            }
+            if (!a.route_only) quantize_tokens_warp(a);
+            {
+                // warm the top-k code on this SM (the last router CTA runs it for real)
+                uint8_t *scratch = sm.slot(0) + (size_t)NSLOT * SLOT_BYTES - 8192;
+                float *sc_w = reinterpret_cast<float *>(scratch);                    // [MAX_E]
+                int16_t *ri = reinterpret_cast<int16_t *>(scratch + 4 * MAX_E);        // [MAX_K]
+                int16_t *po = ri + MAX_K;                                              // [MAX_K]
+                float *rw = reinterpret_cast<float *>(po + MAX_K);                     // [MAX_K]
+                if (a.E <= 256) topk_token<8>(a, 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
+                else topk_token<MAX_E / 32>(a, 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
+            }
+            return;
+        }
         produce(sm, i0, i1, a.err, decode);
         return;
     }
-    if (a.tc && !a.route_only) quantize_tokens(a);
-    router_logits(a, sm);
+    const __nv_bfloat16 *xsm = nullptr;
+    if (stage_x && wf_wait(sm.full(0), 0, a.err)) xsm = reinterpret_cast<const __nv_bfloat16 *>(sm.slot(0));
+    router_logits(a, sm, xsm);
     __threadfence();
     bar_sync(1, NCT);
     const unsigned nrc = min((unsigned)a.E, gridDim.x);
