@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     int *rt_s = reinterpret_cast<int *>(base + OFF_ROUTE);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, 1); }
+        // empty: every issuer releases every stage use (see the issuer loop)
+        for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, NISS); }
         mbar_init(B.b_ready, 4);
         mbar_init(B.b_free, NISS);
         for (int j = 0; j < 2; ++j) {
@@ -307,9 +308,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     if (j == sg.j0 || gj == 0) {
                         if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort)) { ok = false; break; }
                     }
-                    if (own == ii) {
-                        const int st = gs & (STAGES - 1);
-                        if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
+                    // Every issuer waits for every stage use, not only its own: a parity
+                    // wait is valid only while the barrier is at most one phase away,
+                    // and an issuer that skipped the previous use of this stage could
+                    // otherwise see its still-pending phase as this one's.  Non-owners
+                    // release the use at once; the producer refills a stage when all
+                    // issuers have passed it and the owner's MMAs are done.
+                    const int st = gs & (STAGES - 1);
+                    if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
+                    if (own != ii) {
+                        mbar_arrive(B.empty + st);
+                    } else {
                         tc::fence_after_sync();
                         const uint64_t ad = a0 + (uint64_t)((st * STAGE_BYTES) >> 4);
                         const uint64_t bd = b0 + (uint64_t)((j * BSTEP) >> 4);
