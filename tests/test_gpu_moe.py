@@ -138,6 +138,23 @@ def test_batch_consistency_config2(engine):
         U.assert_layer_close_envelope(U.to_f32(y), y_ref, y_ref32, what)
 
 
+@pytest.mark.parametrize("spec", [F.CONFIG1, ORACLE_SPECS[1]], ids=["config1", "D512"])
+def test_repeated_calls_bit_identical(spec, engine):
+    """30 calls on one layer give bit-identical outputs: the stream-K split, the
+    issuer order and every fixed-order sum are deterministic, and a pipeline race
+    (a stage read before its copy landed) shows up as a differing call."""
+    syn = _syn(spec)
+    dl = _layer(spec, list(range(spec.E)))
+    for T in (8, 13):
+        x16, _ = syn.activations(T, draw=5)
+        x = U.bf16_tensor(x16)
+        ys = [dl.forward(x).clone() for _ in range(30)]
+        torch.cuda.synchronize()
+        dl.read_error()
+        bad = [i for i in range(1, len(ys)) if not torch.equal(ys[i], ys[0])]
+        assert not bad, f"T={T}: calls {bad[:5]} differ from the first"
+
+
 def test_expert_parallel_partials_match_oracle():
     """Two expert shards, summed partials + shared (architecture.py:785-793) vs the oracle."""
     spec = F.LayerSpec(D=512, I=256, E=16, topk=4, score_func="sigmoid", route_scale=1.5, seed=41)

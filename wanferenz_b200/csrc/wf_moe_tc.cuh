@@ -38,17 +38,19 @@ namespace mtc {
 constexpr int W_PROD = 4, W_ISS0 = 5, NISS = 3;
 constexpr int THREADS = 8 * 32;
 constexpr int NWK = 128;                 // worker threads
-constexpr int STAGES = 4;
+constexpr int MAX_STAGES = 6;            // stage barriers provided
 constexpr int STAGE_BYTES = 32768;
 constexpr int TILE_BYTES = 16384;
 constexpr int NT = 16;                   // tokens per item (MMA N)
 constexpr int BSTEP = NT * 128;          // B bytes per K step
 constexpr int MAX_STEPS = 32;            // K <= 4096
 constexpr int GRP = 8;                   // K steps per weight-scale group
+// The weight stages and the B operand share one region: B takes nst x BSTEP
+// (all K steps of a token group), the stages the rest (4 at K = 4096, 5 at 2048).
 constexpr int OFF_A = 0;
-constexpr int OFF_B = STAGES * STAGE_BYTES;
-constexpr int OFF_BAR = OFF_B + MAX_STEPS * BSTEP;
-constexpr int NBAR = 2 * STAGES + 10 + NISS;  // ..., fin[NISS]
+constexpr int AB_BYTES = 4 * STAGE_BYTES + MAX_STEPS * BSTEP;  // stages, then B (192 KB)
+constexpr int OFF_BAR = OFF_A + AB_BYTES;
+constexpr int NBAR = 2 * MAX_STAGES + 10 + NISS;  // ..., fin[NISS]
 constexpr int OFF_MISC = (OFF_BAR + NBAR * 8 + 127) / 128 * 128;
 constexpr int AM_LD = NT + 4;                    // amax tile row: 16-byte aligned, conflict-free reads
 constexpr int OFF_EX = OFF_MISC + 128;           // [128 rows][AM_LD] |h|, then [NT] scales
@@ -86,14 +88,14 @@ __device__ __forceinline__ Bars bars_at(uint8_t *base) {
     uint64_t *b = reinterpret_cast<uint64_t *>(base + OFF_BAR);
     Bars r;
     r.full = b;
-    r.empty = b + STAGES;
-    r.b_ready = b + 2 * STAGES;
-    r.b_free = b + 2 * STAGES + 1;
-    r.sfa_ready = b + 2 * STAGES + 2;  // [2]
-    r.sfa_free = b + 2 * STAGES + 4;   // [2]
-    r.d_ready = b + 2 * STAGES + 6;    // [2]
-    r.d_free = b + 2 * STAGES + 8;     // [2]
-    r.fin = b + 2 * STAGES + 10;       // [NISS] issuer drain
+    r.empty = b + MAX_STAGES;
+    r.b_ready = b + 2 * MAX_STAGES;
+    r.b_free = b + 2 * MAX_STAGES + 1;
+    r.sfa_ready = b + 2 * MAX_STAGES + 2;  // [2]
+    r.sfa_free = b + 2 * MAX_STAGES + 4;   // [2]
+    r.d_ready = b + 2 * MAX_STAGES + 6;    // [2]
+    r.d_free = b + 2 * MAX_STAGES + 8;     // [2]
+    r.fin = b + 2 * MAX_STAGES + 10;       // [NISS] issuer drain
     return r;
 }
 
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         // empty: every issuer releases every stage use (see the issuer loop)
-        for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, NISS); }
+        for (int s = 0; s < MAX_STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, NISS); }
         mbar_init(B.b_ready, 4);
         mbar_init(B.b_free, NISS);
         for (int j = 0; j < 2; ++j) {
@@ -231,6 +233,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     const int D = a.D, I = a.I;
     const int K = PH == 2 ? D : I;
     const int nst = K / 128;
+    // stages: what the B operand leaves of the shared region
+    const int nstg = min(MAX_STAGES, (AB_BYTES - nst * BSTEP) / STAGE_BYTES);
+    uint8_t *const Bbase = base + OFF_A + nstg * STAGE_BYTES;
     const int n_items = r.ns + (PH == 2 ? a.hdr[H_IT2] : a.hdr[H_IT3]);
     const long long S = (long long)n_items * nst;
     const int G = gridDim.x;
@@ -251,13 +256,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         if (lane == 0) {
             TCursor cur;
             Seg sg{0, 0, 0, -1};
-            int gs = 0;
+            int gs = 0, st = 0, lap = 0;  // step count; its stage and ring lap
             while (!*abort && next_seg(sg)) {
                 const TItem it = decode<PH>(a, r, cur, sg.i);
                 const uint32_t tx = it.shared ? STAGE_BYTES : STAGE_BYTES / 2;
-                for (int j = sg.j0; j < sg.j1; ++j, ++gs) {
-                    const int st = gs & (STAGES - 1);
-                    if (gs >= STAGES && !twait(B.empty + st, ((gs / STAGES) - 1) & 1, a.err, abort)) break;
+                for (int j = sg.j0; j < sg.j1; ++j, ++gs, lap += (st + 1 == nstg), st = (st + 1 == nstg) ? 0 : st + 1) {
+                    if (gs >= nstg && !twait(B.empty + st, (lap - 1) & 1, a.err, abort)) break;
                     uint8_t *dst = base + OFF_A + st * STAGE_BYTES;
                     mbar_arrive_expect_tx(B.full + st, tx);
                     if (PH == 2) {
@@ -270,9 +274,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 }
             }
             // every issued copy lands before the CTA may exit
-            for (int k = 0; k < STAGES && k < gs; ++k) {
-                const int g = gs - 1 - k, st = g & (STAGES - 1);
-                wf_wait(B.full + st, (g / STAGES) & 1, a.err);
+            for (int k = 0; k < nstg && k < gs; ++k) {
+                const int g = gs - 1 - k;
+                wf_wait(B.full + g % nstg, (g / nstg) & 1, a.err);
             }
         }
     } else if (warp >= W_ISS0) {
@@ -282,8 +286,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
             TCursor cur;
             Seg sg{0, 0, 0, -1};
             int gs = 0, gi = 0, nb = 0, key = -1;
+            int st = 0, lap = 0;  // stage and ring lap of step gs
             const uint64_t a0 = tc::smem_desc_sw128(base + OFF_A);
-            const uint64_t b0 = tc::smem_desc_sw128(base + OFF_B);
+            const uint64_t b0 = tc::smem_desc_sw128(Bbase);
             bool more = next_seg(sg);
             while (more && !*abort) {
                 const TItem it = decode<PH>(a, r, cur, sg.i);
@@ -302,7 +307,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 bool first = true;
                 bool ok = true;
                 int own = 0;  // issuer of step j: (j - j0) mod NISS
-                for (int j = sg.j0; j < sg.j1; ++j, ++gs, own = (own + 1 == NISS) ? 0 : own + 1) {
+                for (int j = sg.j0; j < sg.j1; ++j, ++gs, own = (own + 1 == NISS) ? 0 : own + 1,
+                                                lap += (st + 1 == nstg), st = (st + 1 == nstg) ? 0 : st + 1) {
                     // weight-scale groups: K steps [8k, 8k+8) of the item, cut to the segment
                     const int gj = j & (GRP - 1);
                     if (j == sg.j0 || gj == 0) {
@@ -314,8 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     // otherwise see its still-pending phase as this one's.  Non-owners
                     // release the use at once; the producer refills a stage when all
                     // issuers have passed it and the owner's MMAs are done.
-                    const int st = gs & (STAGES - 1);
-                    if (!twait(B.full + st, (gs / STAGES) & 1, a.err, abort)) { ok = false; break; }
+                    if (!twait(B.full + st, lap & 1, a.err, abort)) { ok = false; break; }
                     if (own != ii) {
                         mbar_arrive(B.empty + st);
                     } else {
@@ -361,7 +366,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         TCursor cur, cur_e;
         Seg sg{0, 0, 0, -1};
         int gi = 0, nb = 0, key = -1;
-        uint8_t *Bsm = base + OFF_B;
+        uint8_t *Bsm = Bbase;
         // The four worker warps share named barriers, so each wait ends in one
         // decision for all of them: a timeout seen by any warp stops every warp.
         bool dead = false;
