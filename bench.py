@@ -212,8 +212,11 @@ def kernel_names():
 MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 759.0e6, "k_moe_tc<3>": 389.6e6}
 
 
-def step_bytes(indices, T, e0, El):
-    """Bytes each kernel must move at minimum, given this step's expert indices [T, k]."""
+def step_bytes(indices, T, e0, El, router=True, shared=True):
+    """Bytes each kernel must move at minimum, given this step's expert indices [T, k].
+
+    ``router=False`` drops the gate (routing given); ``shared=False`` drops the
+    shared expert (its weights and its activation traffic)."""
     import numpy as np
 
     idx = np.asarray(indices)
@@ -222,19 +225,40 @@ def step_bytes(indices, T, e0, El):
     pairs = sum(len(set(r[(r >= e0) & (r < e0 + El)].tolist())) for r in idx)
     w13 = 2 * I * (D // 2 + D // 32)
     w2 = D * (I // 2 + I // 32)
-    s13 = 2 * I * D + 2 * (I // 128) * (D // 128)
-    s2 = D * I + (D // 128) * (I // 128)
+    s13 = (2 * I * D + 2 * (I // 128) * (D // 128)) if shared else 0
+    s2 = (D * I + (D // 128) * (I // 128)) if shared else 0
+    Ts = T if shared else 0
+    rb = ROUTER_BYTES if router else T * idx.shape[1] * 12
     n1, n2, n3 = kernel_names()
     if tc_engine():
         # router + token quantization | routed + shared w1/w3 -> E4M3 hidden | w2 + combine
-        k1 = ROUTER_BYTES + T * D * 2 + T * D + T * D // 128
-        k2 = n_exp * w13 + s13 + T * D + pairs * I + T * I
-        k3 = n_exp * w2 + s2 + pairs * I + T * I + (pairs + T) * D * 2 * 2 + T * D * 2
+        k1 = rb + T * D * 2 + T * D + T * D // 128
+        k2 = n_exp * w13 + s13 + T * D + pairs * I + Ts * I
+        k3 = n_exp * w2 + s2 + pairs * I + Ts * I + (pairs + Ts) * D * 2 * 2 + T * D * (2 if shared else 4)
     else:
-        k1 = ROUTER_BYTES + s13 + T * D * 2 + T * I * 2
-        k2 = n_exp * w13 + s2 + T * D * 2 + pairs * I * 2 + T * I * 2 + T * D * 2
+        k1 = rb + s13 + T * D * 2 + Ts * I * 2
+        k2 = n_exp * w13 + s2 + T * D * 2 + pairs * I * 2 + Ts * I * 2 + Ts * D * 2
         k3 = n_exp * w2 + pairs * I * 2 + pairs * D * 2 * 2 + T * D * 2 * 2
     return {n1: k1, n2: k2, n3: k3, "experts": n_exp, "pairs": pairs}
+
+
+EP_PHASES = ["own_route_shared", "all_gather", "routed_experts", "reduce_scatter", "add_shared"]
+
+
+def ep_step_bytes(idx_g, Tloc, world, e0, El):
+    """Per-phase bytes of one expert-parallel step (``wanferenz_b200.ep.ep_forward``)."""
+    import numpy as np
+
+    own = step_bytes(np.zeros((Tloc, K_TOP), np.int64) - 1, Tloc, e0, El)
+    rt = step_bytes(idx_g, Tloc * world, e0, El, router=False, shared=False)
+    names = kernel_names()
+    tok = 2 * D + 12 * K_TOP
+    return {"own_route_shared": sum(own[k] for k in names),
+            "all_gather": (world - 1) * Tloc * tok,            # bytes each rank receives
+            "routed_experts": sum(rt[k] for k in names),
+            "reduce_scatter": (world - 1) * Tloc * D * 4,      # bytes each rank receives
+            "add_shared": Tloc * D * (4 + 2 + 2),
+            "experts": rt["experts"], "pairs": rt["pairs"]}
 
 
 # ---------------------------------------------------------------------------
@@ -248,6 +272,7 @@ def run_gpu(args):
     import torch.distributed as dist
 
     from wanferenz_b200 import _lib as L
+    from wanferenz_b200 import ep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -283,29 +308,56 @@ def run_gpu(args):
             for e in row:
                 e.record()
         xg = [torch.empty(Tgl, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
+        wg = [torch.empty(Tgl, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
         part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]
         mine = [torch.empty(Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
+        sh = [torch.empty(Tloc, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
+        rw = [torch.empty(Tloc, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
+        ri = [torch.empty(Tloc, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
+        pev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(EP_PHASES) + 1)] for _ in range(n)]
+
+        def one_ep(i, timed=False):
+            """Token-owner split (wanferenz_b200.ep.ep_forward) through the C ABI."""
+            lay = layers[i % len(layers)]
+            st = L.stream_ptr()
+            cfg, wst, ws, wsn = ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(lay.workspace), \
+                lay.workspace.numel()
+            ev = pev[i] if timed else None
+            if ev:
+                ev[0].record()
+            L.check(lib.wf_moe_forward_ep(cfg, wst, L.ptr(xs[i]), None, Tloc, L.WF_EP_SHARED_ONLY, None, None,
+                                          L.ptr(sh[i]), None, L.ptr(rw[i]), L.ptr(ri[i]), ws, wsn, st),
+                    "wf_moe_forward_ep")
+            if ev:
+                ev[1].record()
+            ep.gather_tokens(xs[i], rw[i], ri[i], xg[i], wg[i], idx[i])
+            if ev:
+                ev[2].record()
+            L.check(lib.wf_moe_forward_ep(cfg, wst, L.ptr(xg[i]), None, Tgl, L.WF_EP_ROUTED_ONLY, L.ptr(wg[i]),
+                                          L.ptr(idx[i]), None, L.ptr(part[i]), None, None, ws, wsn, st),
+                    "wf_moe_forward_ep")
+            if ev:
+                ev[3].record()
+            dist.reduce_scatter_tensor(mine[i], part[i])
+            if ev:
+                ev[4].record()
+            L.check(lib.wf_moe_add_shared(L.ptr(mine[i]), L.ptr(sh[i]), Tloc * D, L.ptr(ys[i]), st),
+                    "wf_moe_add_shared")
+            if ev:
+                ev[5].record()
 
         def one(i, timed=False):
+            if world > 1:
+                return one_ep(i, timed)
             lay = layers[i % len(layers)]
             st = L.stream_ptr()
             ev = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in evs[i]])
-            x_in, T_in = (xs[i], Tloc) if world == 1 else (xg[i], Tgl)
-            if world > 1:
-                dist.all_gather_into_tensor(xg[i], xs[i])
-            args_ = (ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(x_in), 0, T_in,
-                     L.ptr(ys[i]) if world == 1 else 0, 0 if world == 1 else L.ptr(part[i]), 0,
-                     L.ptr(idx[i]), L.ptr(lay.workspace), lay.workspace.numel(), st)
+            args_ = (ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(xs[i]), 0, Tloc,
+                     L.ptr(ys[i]), 0, 0, L.ptr(idx[i]), L.ptr(lay.workspace), lay.workspace.numel(), st)
             if timed:
                 L.check(lib.wf_moe_forward_timed(*args_, ev), "wf_moe_forward_timed")
             else:
                 L.check(lib.wf_moe_forward(*args_), "wf_moe_forward")
-            if world > 1:
-                dist.reduce_scatter_tensor(mine[i], part[i])
-                # shared expert rows of this rank + bf16 cast (architecture.py:793-794)
-                L.check(lib.wf_moe_finish(ctypes.byref(lay.cfg), L.ptr(mine[i]), Tloc, rank * Tloc,
-                                          L.ptr(ys[i]), L.ptr(lay.workspace), lay.workspace.numel(), st),
-                        "wf_moe_finish")
 
         for i in range(W):
             one(i)
@@ -342,10 +394,10 @@ def run_gpu(args):
             one(i, timed=True)
         torch.cuda.synchronize()
         del big
-        names = kernel_names()
+        names = kernel_names() if world == 1 else EP_PHASES
         kern = {k: [] for k in names}
         for i in range(W, n):
-            e = evs[i]
+            e = evs[i] if world == 1 else pev[i]
             for j, k in enumerate(names):
                 kern[k].append(e[j].elapsed_time(e[j + 1]))
         routing = [idx[i].cpu().numpy() for i in range(W, n)]
@@ -360,10 +412,14 @@ def run_gpu(args):
         total_ms = float(t.item())
         ms = total_ms / K
         lay0 = layers[0]
-        byts = [step_bytes(r, Tloc * world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
+        if world == 1:
+            byts = [step_bytes(r, Tloc, lay0.expert_offset, lay0.n_local_experts) for r in routing]
+        else:
+            byts = [ep_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
-        layer_bytes = sum(mean[k] for k in kernel_names())
+        layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else
+                                            ["own_route_shared", "routed_experts", "add_shared"]))
         hist = [np.bincount(r.ravel(), minlength=E) for r in routing]
         tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
                "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
@@ -388,7 +444,9 @@ def run_gpu(args):
             }
     # dominant kernel roofline
     kms = main["kms"]
-    dom = max(kms, key=kms.get)
+    # the dominant HBM-bound kernel (multi-GPU: of the compute phases; the collectives
+    # are reported in kernel_us beside them)
+    dom = max((k for k in kms if k not in ("all_gather", "reduce_scatter")), key=kms.get)
     ach = main["bytes"][dom] / (kms[dom] * 1e-3) / 1e9
     value = T * world / (main["ms"] * 1e-3)
     traffic, traffic_src = None, None
@@ -428,7 +486,9 @@ def run_gpu(args):
                      "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
         "clocks": main["clocks"],
-        "gpu_launches": 3 * args.steps if world == 1 else 4 * args.steps,
+        # single GPU: K1 + two expert phases; multi-GPU: the same three for the own
+        # tokens (router + shared) and for the gathered batch (routed), plus add_shared
+        "gpu_launches": 3 * args.steps if world == 1 else 7 * args.steps,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

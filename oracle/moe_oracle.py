@@ -344,7 +344,8 @@ def _swiglu(g, u, weights, limit):
     return round_bf16(h)
 
 
-def moe_forward(x, params, input_ids=None, expert_range=None, acc=np.float64, return_partial=False):
+def moe_forward(x, params, input_ids=None, expert_range=None, acc=np.float64, return_partial=False,
+                routing=None):
     """``MoE.forward`` (architecture.py:777-794).
 
     ``x`` float32 ``[T, D]`` bf16-valued.  ``params`` is a dict:
@@ -359,13 +360,19 @@ def moe_forward(x, params, input_ids=None, expert_range=None, acc=np.float64, re
     of its last slot (index-put semantics, fp4_grouped.py:265-268).
     ``expert_range=(lo, hi)`` restricts to one expert-parallel shard (749-756);
     with ``return_partial`` the fp32 routed partial sum is returned before the
-    all-reduce and shared expert (791-793).
+    all-reduce and shared expert (791-793).  ``routing=(weights, indices)``
+    replaces the gate with a routing computed elsewhere (the expert-parallel
+    split routes each token once, on the rank that owns it).
     Returns ``(y bf16-valued float32 [T, D], weights, indices)``.
     """
     T, D = x.shape
-    weights, indices, _ = gate(
-        x, params["gate_w"], params.get("gate_b"), params["topk"], params["score_func"],
-        params["route_scale"], params.get("tid2eid"), input_ids, acc)
+    if routing is not None:
+        weights = np.asarray(routing[0], np.float32)
+        indices = np.asarray(routing[1], np.int64)
+    else:
+        weights, indices, _ = gate(
+            x, params["gate_w"], params.get("gate_b"), params["topk"], params["score_func"],
+            params["route_scale"], params.get("tid2eid"), input_ids, acc)
     E = params["gate_w"].shape[0]
     lo, hi = expert_range if expert_range is not None else (0, E)
     y = np.zeros((T, D), np.float32)

@@ -107,6 +107,11 @@ struct MoeArgs {
     Geo g;
     int tc;              // expert phases on tcgen05 (k_moe_tc): K1 quantizes x, skips the shared expert
     uint8_t *xq, *xs;    // E4M3 tokens [T, D] and their e8m0 scales [T, D/128] (tc)
+    // expert-parallel split (wf_moe_forward_ep): 0 whole layer; WF_EP_SHARED_ONLY route
+    // and shared expert only; WF_EP_ROUTED_ONLY given routing, local routed experts only
+    int ep_mode;
+    const float *in_w;         // [T, topk] given routing weights (routed-only)
+    const long long *in_idx;   // [T, topk] given expert indices (routed-only)
 };
 
 // Dense GEMM (operator entry points) arguments.
@@ -922,13 +927,34 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
     unsigned long long *scan_ws = reinterpret_cast<unsigned long long *>(off_s + MAX_E);   // [NCW]
     const int TW = (T + 31) >> 5;
     // ---- 1. top-k: one warp per token, scores of the warp's token in shared memory
-    float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);  // [NCW][MAX_E]
-    for (int t = warp; t < T; t += NCW) {
-        if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
-        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+    // (routed-only calls take the routing computed by the ranks that own the tokens)
+    if (a.ep_mode == WF_EP_ROUTED_ONLY) {
+        for (int slot = tid; slot < T * K; slot += NCT) {
+            long long e = __ldg(a.in_idx + slot);
+            if (e < 0 || e >= E) { atomicOr(a.err, kErrExpertId); e = 0; }
+            ridx_s[slot] = (int16_t)e;
+            rw_s[slot] = __ldg(a.in_w + slot);
+            pof_s[slot] = -1;
+        }
+    } else {
+        float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);  // [NCW][MAX_E]
+        for (int t = warp; t < T; t += NCW) {
+            if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+            else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        }
     }
     bar_sync(1, NCT);
     if (a.route_only) {
+        __threadfence();
+        return;
+    }
+    if (a.ep_mode == WF_EP_SHARED_ONLY) {
+        // no routed work: empty dispatch tables, so only the shared expert runs
+        if (tid == 0) {
+            a.act_off[0] = 0; a.act_it2[0] = 0; a.act_it3[0] = 0;
+            a.hdr[H_NACT] = 0; a.hdr[H_IT2] = 0; a.hdr[H_IT3] = 0; a.hdr[H_TGT] = 0; a.hdr[H_NPAIR] = 0;
+        }
+        for (int t = tid; t < T; t += NCT) a.tok_np[t] = 0;
         __threadfence();
         return;
     }
@@ -1184,14 +1210,15 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     init_smem(sm);
     pdl_wait();
     pdl_launch_dependents();
-    const int n = (a.route_only || a.tc) ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
+    const bool given = a.ep_mode == WF_EP_ROUTED_ONLY;
+    const int n = (a.route_only || a.tc || given) ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0, nullptr, nullptr, nullptr); };
     // tcgen05 mode: the ring is idle, so up to TPI token rows are staged in it with
     // one bulk copy for the router, and the producer warp quantizes the tokens
     const size_t xbytes = (size_t)a.T * a.D * 2;
-    const bool stage_x = a.tc && a.T <= TPI && xbytes + 8192 <= (size_t)NSLOT * SLOT_BYTES &&
+    const bool stage_x = a.tc && !given && a.T <= TPI && xbytes + 8192 <= (size_t)NSLOT * SLOT_BYTES &&
                          blockIdx.x < (unsigned)a.E;
     if ((threadIdx.x >> 5) == NCW) {
         if (a.tc) {
@@ -1200,7 +1227,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
                 bulk_g2s(sm.slot(0), a.x, (uint32_t)xbytes, sm.full(0));
             }
             if (!a.route_only) quantize_tokens_warp(a);
-            {
+            if (!given) {
                 // warm the top-k code on this SM (the last router CTA runs it for real)
                 uint8_t *scratch = sm.slot(0) + (size_t)NSLOT * SLOT_BYTES - 8192;
                 float *sc_w = reinterpret_cast<float *>(scratch);                    // [MAX_E]
@@ -1215,6 +1242,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
         produce(sm, i0, i1, a.err, decode);
         return;
     }
+    if (given) {
+        // routing given: no router; CTA 0 builds the dispatch tables
+        if (blockIdx.x == 0) topk_dispatch(a, sm);
+    } else {
     const __nv_bfloat16 *xsm = nullptr;
     if (stage_x && wf_wait(sm.full(0), 0, a.err)) xsm = reinterpret_cast<const __nv_bfloat16 *>(sm.slot(0));
     router_logits(a, sm, xsm);
@@ -1233,6 +1264,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
             if (threadIdx.x == 0) *a.cnt_router = 0u;
         }
         bar_sync(1, NCT);
+    }
     }
     MoeRowPtr rp{&a, nullptr};
     auto f8 = [&](int rblk, int kb) {
@@ -1260,7 +1292,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
     const int n_act = a.hdr[H_NACT], n_it2 = a.hdr[H_IT2];
     load_route(sm, a.act_expert, a.act_off, a.act_it2, a.pair_tok, a.pair_w, n_act, a.hdr[H_NPAIR]);
     const RouteSm rt = route_sm(sm);
-    const int n = n_it2 + (a.D / a.g.rs2) * cdiv(a.T, TPI);
+    const int n = n_it2 + (a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : (a.D / a.g.rs2) * cdiv(a.T, TPI));
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&, c = Cursor{-1, 0}](int i) mutable {
@@ -1948,6 +1980,40 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
     return launch_moe(a, false, (cudaStream_t)stream, events, &t);
 }
 
+int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                      const int64_t *input_ids, int32_t T, int32_t mode, const float *in_weights,
+                      const int64_t *in_indices, void *y, float *y_partial, float *out_weights,
+                      int64_t *out_indices, void *workspace, size_t workspace_bytes, void *stream) {
+    if (mode != WF_EP_SHARED_ONLY && mode != WF_EP_ROUTED_ONLY) return fail(WF_E_ARG, "bad expert-parallel mode");
+    int rc = check_expert_ptrs(w);
+    if (rc) return rc;
+    wf::MoeArgs a;
+    wf::mtc::TcArgs t;
+    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
+    if (rc) return rc;
+    a.ep_mode = mode;
+    if (mode == WF_EP_SHARED_ONLY) {
+        if (!y || !out_weights || !out_indices) return fail(WF_E_ARG, "shared-only mode needs y and the routing outputs");
+        a.y = (__nv_bfloat16 *)y; a.y_partial = nullptr; a.partial = 0;
+        a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    } else {
+        if (!y_partial || !in_weights || !in_indices) return fail(WF_E_ARG, "routed-only mode needs y_partial and the routing");
+        a.y = nullptr; a.y_partial = y_partial; a.partial = 1;
+        a.in_w = in_weights; a.in_idx = (const long long *)in_indices;
+        a.out_w = nullptr; a.out_idx = nullptr;
+    }
+    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
+}
+
+int wf_moe_add_shared(const float *y_partial, const void *shared, int64_t n, void *y, void *stream) {
+    if (!y_partial || !shared || !y) return fail(WF_E_ARG, "null pointer");
+    if (n <= 0 || n > (int64_t)1 << 30) return fail(WF_E_SHAPE, "n outside 1..2^30");
+    wf::k_moe_finish<<<(unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, (cudaStream_t)stream>>>(
+        y_partial, (const __nv_bfloat16 *)shared, (__nv_bfloat16 *)y, (int)n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "add_shared launch");
+}
+
 int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
                  const int64_t *input_ids, int32_t T, float *out_weights, int64_t *out_indices,
                  void *workspace, size_t workspace_bytes, void *stream) {
@@ -2046,6 +2112,11 @@ int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *strea
     cudaError_t e = cudaMemcpyAsync(&host, workspace, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "read error word");
+    if (host) {
+        // read-and-clear: the next read reports only what later calls set
+        e = cudaMemsetAsync((void *)workspace, 0, 4, (cudaStream_t)stream);
+        if (e != cudaSuccess) return cuda_fail(e, "clear error word");
+    }
     if (host & wf::kErrTimeout) return fail(WF_E_TIMEOUT, "a device wait timed out");
     if (host & wf::kErrExpertId) return fail(WF_E_EXPERT_ID, "token or expert id out of range");
     return WF_OK;

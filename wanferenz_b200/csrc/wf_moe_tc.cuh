@@ -76,7 +76,7 @@ struct TcArgs {
     const uint8_t *xq, *xs;    // tokens E4M3 [T, D], e8m0 [T, D/128] (router kernel)
     uint8_t *hq, *hqs;         // routed hidden E4M3 [P, I], e8m0 [P, I/128]
     uint8_t *sq, *sqs;         // shared hidden E4M3 [T, I], e8m0 [T, I/128]
-    float *part;               // [2 * grid][2][128][NT] partial slots
+    float *part;               // [2 * grid][2][NT/4][128][4] partial slots (float4 per row and 4 tokens)
     unsigned *cnt;             // [items] segment arrivals
 };
 
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         r.act_it = rt_s + 2 * (MAX_E + 1);
         r.n_act = n_act;
         r.nblk = PH == 2 ? a.I / 128 : a.D / 256;
-        r.ns = r.nblk * cdiv(a.T, NT);
+        r.ns = a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : r.nblk * cdiv(a.T, NT);  // shared items
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -240,6 +240,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     const long long S = (long long)n_items * nst;
     const int G = gridDim.x;
     const long long u0 = cta_start(blockIdx.x, S, G), u1 = cta_start(blockIdx.x + 1, S, G);
+    if (PH == 3 && n_items == 0 && warp < 4) {
+        // no item at all (a routed-only call whose shard got no tokens): the combine
+        // still writes every row block (zeros)
+        for (int rb = blockIdx.x; rb < D / 256; rb += G) combine_rows_v8<NWK>(a, rb * 256, 256);
+    }
     // segment after `sg` (or the first one when sg.q < 0); false at the end of the range
     auto next_seg = [&](Seg &sg) -> bool {
         const long long u = sg.q < 0 ? u0 : (long long)sg.i * nst + sg.j1;
@@ -408,14 +413,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 // segment of the item to arrive sums all of them in segment order
                 const long long is = (long long)e.i * nst;
                 const int mine = blockIdx.x * 2 + (u0 >= is ? 0 : 1);
-                float *ps = t.part + (size_t)mine * (2 * 128 * NT);
+                // slot layout [gate/up][token/4][row][4]: each warp access is 512
+                // contiguous bytes, written here and read back by the fix-up
+                float4 *ps = reinterpret_cast<float4 *>(t.part + (size_t)mine * (2 * 128 * NT));
 #pragma unroll
-                for (int n = 0; n < NT; ++n) {
-                    if ((n & 3) == 0 && n >= ntok) break;
-                    if (n < ntok) {
-                        ps[(0 * 128 + row) * NT + n] = g[n];
-                        ps[(1 * 128 + row) * NT + n] = u[n];
-                    }
+                for (int c = 0; c < NT / 4; ++c) {
+                    if (4 * c >= ntok) break;
+                    ps[c * 128 + row] = make_float4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]);
+                    ps[(NT / 4 + c) * 128 + row] = make_float4(u[4 * c], u[4 * c + 1], u[4 * c + 2], u[4 * c + 3]);
                 }
                 __threadfence();
                 bar_sync(1, NWK);
@@ -435,17 +440,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
 #pragma unroll
                 for (int n = 0; n < NT; ++n) { g[n] = 0.f; u[n] = 0.f; }
                 const int blo = cta_of(is, S, G), bhi = cta_of(is + nst - 1, S, G);
+#pragma unroll 2
                 for (int b = blo; b <= bhi; ++b) {
                     const long long ub = cta_start(b, S, G);
                     if (cta_start(b + 1, S, G) <= ub) continue;
-                    const float *pp = t.part + (size_t)(b * 2 + (ub >= is ? 0 : 1)) * (2 * 128 * NT);
+                    const float4 *pp =
+                        reinterpret_cast<const float4 *>(t.part + (size_t)(b * 2 + (ub >= is ? 0 : 1)) * (2 * 128 * NT));
+                    float4 vg[NT / 4], vu[NT / 4];
 #pragma unroll
-                    for (int n = 0; n < NT; ++n) {
-                        if ((n & 3) == 0 && n >= ntok) break;
-                        if (n < ntok) {
-                            g[n] += __ldcg(pp + (0 * 128 + row) * NT + n);
-                            u[n] += __ldcg(pp + (1 * 128 + row) * NT + n);
-                        }
+                    for (int c = 0; c < NT / 4; ++c) {
+                        if (4 * c >= ntok) break;
+                        vg[c] = __ldcg(pp + c * 128 + row);
+                        vu[c] = __ldcg(pp + (NT / 4 + c) * 128 + row);
+                    }
+#pragma unroll
+                    for (int c = 0; c < NT / 4; ++c) {
+                        if (4 * c >= ntok) break;
+                        g[4 * c] += vg[c].x; g[4 * c + 1] += vg[c].y; g[4 * c + 2] += vg[c].z; g[4 * c + 3] += vg[c].w;
+                        u[4 * c] += vu[c].x; u[4 * c + 1] += vu[c].y; u[4 * c + 2] += vu[c].z; u[4 * c + 3] += vu[c].w;
                     }
                 }
                 if (tid == 0) t.cnt[e.i] = 0u;
@@ -512,7 +524,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 __threadfence();
                 bar_sync(1, NWK);
                 if (tid == 0) {
-                    const unsigned target = (unsigned)(a.hdr[H_TGT] + cdiv(a.T, NT));
+                    const unsigned target =
+                        (unsigned)(a.hdr[H_TGT] + (a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : cdiv(a.T, NT)));
                     const unsigned old = atomicAdd(a.cnt_rb + it.blk, 1u);
                     *flag = old == target - 1;
                 }
