@@ -1071,9 +1071,11 @@ __device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
 // combine_rows with 8 consecutive rows of one token per item (16-byte loads and
 // stores) and two items per thread whose pair lists and pair rows are all
 // loaded before the first add; same fp32 sum in the same order.  nrows and
-// row0 are multiples of 8.
+// row0 are multiples of 8.  With np_s / tp_s (a shared-memory copy of tok_np
+// and tok_pairs) the pair lists cost no global round trip.
 template <int NTH>
-__device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows) {
+__device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows, const uint8_t *np_s = nullptr,
+                                const int16_t *tp_s = nullptr) {
     const int T = a.T, D = a.D, K = a.topk, nv = nrows / 8, n = T * nv;
     for (int base = threadIdx.x; base < n; base += 2 * NTH) {
         int tt[2], rr[2], np[2], pr[2][MAX_K];
@@ -1083,9 +1085,15 @@ __device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows) {
             const bool ok = idx < n;
             tt[j] = ok ? idx / nv : 0;
             rr[j] = row0 + 8 * (ok ? idx - tt[j] * nv : 0);
-            np[j] = ok ? __ldcg(a.tok_np + tt[j]) : 0;
+            if (np_s) {
+                np[j] = ok ? np_s[tt[j]] : 0;
 #pragma unroll
-            for (int q = 0; q < MAX_K; ++q) pr[j][q] = (ok && q < K) ? __ldcg(a.tok_pairs + tt[j] * K + q) : 0;
+                for (int q = 0; q < MAX_K; ++q) pr[j][q] = (ok && q < K) ? tp_s[tt[j] * K + q] : 0;
+            } else {
+                np[j] = ok ? __ldcg(a.tok_np + tt[j]) : 0;
+#pragma unroll
+                for (int q = 0; q < MAX_K; ++q) pr[j][q] = (ok && q < K) ? __ldcg(a.tok_pairs + tt[j] * K + q) : 0;
+            }
         }
         uint4 v[2][MAX_K];
 #pragma unroll

@@ -45,6 +45,10 @@ constexpr int NT = 16;                   // tokens per item (MMA N)
 constexpr int BSTEP = NT * 128;          // B bytes per K step
 constexpr int MAX_STEPS = 32;            // K <= 4096
 constexpr int GRP = 8;                   // K steps per weight-scale group
+// Stream-K takes at least this many K steps per CTA: with little work (the
+// shared expert alone, a few tokens) a finer split only adds partial-sum
+// fix-ups to the end of the kernel, which cost more than the streaming they save.
+constexpr int MIN_SEG = 16;
 // The weight stages and the B operand share one region: B takes nst x BSTEP
 // (all K steps of a token group), the stages the rest (4 at K = 4096, 5 at 2048).
 constexpr int OFF_A = 0;
@@ -57,7 +61,10 @@ constexpr int OFF_EX = OFF_MISC + 128;           // [128 rows][AM_LD] |h|, then 
 constexpr int EX_BYTES = (128 * AM_LD + 2 * NT) * 4;
 constexpr int OFF_ROUTE = OFF_EX + EX_BYTES;     // act_expert, act_off, act_it
 constexpr int ROUTE_BYTES = 3 * (MAX_E + 1) * 4;
-constexpr int SMEM = OFF_ROUTE + ROUTE_BYTES + 1024;  // + alignment slack
+constexpr int OFF_TOK = OFF_ROUTE + ROUTE_BYTES;  // w2 phase: tok_pairs (int16), then tok_np (uint8)
+constexpr int TOK_BYTES = MAX_T * MAX_K * 2 + MAX_T;
+constexpr int SMEM = OFF_TOK + TOK_BYTES + 1024;  // + alignment slack
+static_assert(MAX_PAIRS <= 32767, "pair indices fit int16");
 static_assert(SMEM <= 232448, "shared memory budget");
 static_assert(OFF_EX % 16 == 0 && (AM_LD * 4) % 16 == 0, "float4 rows of the amax tile");
 // TMEM columns (512 allocated)
@@ -190,6 +197,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_MISC) + 2;
     float *ex = reinterpret_cast<float *>(base + OFF_EX);
     int *rt_s = reinterpret_cast<int *>(base + OFF_ROUTE);
+    int16_t *tp_s = reinterpret_cast<int16_t *>(base + OFF_TOK);
+    uint8_t *np_s = base + OFF_TOK + MAX_T * MAX_K * 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         // empty: every issuer releases every stage use (see the issuer loop)
@@ -224,6 +233,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         r.n_act = n_act;
         r.nblk = PH == 2 ? a.I / 128 : a.D / 256;
         r.ns = a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : r.nblk * cdiv(a.T, NT);  // shared items
+        if (PH == 3) {
+            // the combine's pair lists (written by the router kernel)
+            for (int k = threadIdx.x; k < a.T * a.topk; k += THREADS) tp_s[k] = (int16_t)__ldcg(a.tok_pairs + k);
+            for (int k = threadIdx.x; k < a.T; k += THREADS) np_s[k] = (uint8_t)__ldcg(a.tok_np + k);
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -238,12 +252,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     uint8_t *const Bbase = base + OFF_A + nstg * STAGE_BYTES;
     const int n_items = r.ns + (PH == 2 ? a.hdr[H_IT2] : a.hdr[H_IT3]);
     const long long S = (long long)n_items * nst;
-    const int G = gridDim.x;
-    const long long u0 = cta_start(blockIdx.x, S, G), u1 = cta_start(blockIdx.x + 1, S, G);
+    // the CTAs that share the S steps (the others have none)
+    const int G = (int)max(1LL, min((long long)gridDim.x, S / MIN_SEG));
+    const long long u0 = min(S, cta_start(blockIdx.x, S, G)), u1 = min(S, cta_start(blockIdx.x + 1, S, G));
     if (PH == 3 && n_items == 0 && warp < 4) {
         // no item at all (a routed-only call whose shard got no tokens): the combine
         // still writes every row block (zeros)
-        for (int rb = blockIdx.x; rb < D / 256; rb += G) combine_rows_v8<NWK>(a, rb * 256, 256);
+        for (int rb = blockIdx.x; rb < D / 256; rb += gridDim.x) combine_rows_v8<NWK>(a, rb * 256, 256, np_s, tp_s);
     }
     // segment after `sg` (or the first one when sg.q < 0); false at the end of the range
     auto next_seg = [&](Seg &sg) -> bool {
@@ -534,7 +549,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 bar_sync(1, NWK);
                 if (last) {
                     __threadfence();
-                    combine_rows_v8<NWK>(a, it.blk * 256, 256);
+                    combine_rows_v8<NWK>(a, it.blk * 256, 256, np_s, tp_s);
                     if (tid == 0) a.cnt_rb[it.blk] = 0u;
                 }
             }
