@@ -817,11 +817,13 @@ template <int NE>
 __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float *sc_w, int16_t *ridx_s,
                                         int16_t *pof_s, float *rw_s, bool dry) {
     const int E = a.E, K = a.topk;
-    float sc[NE], bs[NE];
+    float sc[NE], bs[NE], gb[NE];
+    // logits and gate bias in one round trip
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
         const int e = lane + 32 * i;
         sc[i] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        gb[i] = (e < E && a.gate_b) ? __ldg(a.gate_b + e) : 0.f;
     }
     if (a.score_func == WF_SCORE_SOFTMAX) {
         float mx = -INFINITY;
@@ -853,7 +855,7 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
         const int e = lane + 32 * i;
-        bs[i] = e < E ? (a.gate_b ? sc[i] + __ldg(a.gate_b + e) : sc[i]) : -INFINITY;
+        bs[i] = e < E ? (a.gate_b ? sc[i] + gb[i] : sc[i]) : -INFINITY;
         if (e < E) sc_w[e] = sc[i];
     }
     long long id = 0;
@@ -861,27 +863,49 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
         id = __ldg(a.ids + t);
         if (id < 0 || id >= a.vocab) { if (lane == 0 && !dry) atomicOr(a.err, kErrExpertId); id = 0; }
     }
+    if (a.hash) {
 #pragma unroll 1
-    for (int j = 0; j < K; ++j) {
-        int ej;
-        if (a.hash) {
-            ej = __ldg(a.tid2eid + id * K + j);
+        for (int j = 0; j < K; ++j) {
+            int ej = __ldg(a.tid2eid + id * K + j);
             if (ej < 0 || ej >= E) { if (lane == 0 && !dry) atomicOr(a.err, kErrExpertId); ej = 0; }
-        } else {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int i = 0; i < NE; ++i) {
-                const int e = lane + 32 * i;
-                if (e < E && (bs[i] > bv || (bs[i] == bv && e < bi))) { bv = bs[i]; bi = e; }
-            }
-            warp_argmax(bv, bi);
-            ej = (bi >= 0 && bi < E) ? bi : 0;  // a dry pass may see non-finite scores
-#pragma unroll
-            for (int i = 0; i < NE; ++i)
-                if (lane + 32 * i == ej) bs[i] = -INFINITY;
+            if (lane == 0) ridx_s[t * K + j] = (int16_t)ej;
         }
-        if (lane == 0) ridx_s[t * K + j] = (int16_t)ej;
+    } else {
+        // Biased scores as unsigned keys with the float order (+0 for -0, so equal
+        // scores give equal keys); 0 marks an expert that is taken or absent.  Each
+        // round takes the largest key, the lowest expert id among equal keys (torch
+        // topk order), with two warp reductions; only the winning lane rescans its
+        // candidates.
+        uint32_t key[NE];
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            uint32_t u = __float_as_uint(bs[i] + 0.0f);
+            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            key[i] = (lane + 32 * i < E) ? u : 0u;
+        }
+        auto best = [&](uint32_t &bk, int &be) {
+            bk = key[0];
+            be = lane;
+#pragma unroll
+            for (int i = 1; i < NE; ++i)
+                if (key[i] > bk) { bk = key[i]; be = lane + 32 * i; }  // ties keep the lower id
+        };
+        uint32_t bk;
+        int be;
+        best(bk, be);
+#pragma unroll 1
+        for (int j = 0; j < K; ++j) {
+            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+            const int w = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)be : 0xffffffffu);
+            const int ej = (w >= 0 && w < E) ? w : 0;  // a dry pass may see any bits
+            if (be == w) {
+#pragma unroll
+                for (int i = 0; i < NE; ++i)
+                    if (lane + 32 * i == w) key[i] = 0u;
+                best(bk, be);
+            }
+            if (lane == 0) ridx_s[t * K + j] = (int16_t)ej;
+        }
     }
     __syncwarp();
     float wj = 0.f;
