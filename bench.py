@@ -11,11 +11,11 @@ cold in L2 (8 layers x ~27 MB of router + shared weights alone > 126 MB L2);
 no L2 flush is used.
 
 N > 1 (torchrun, one rank per GPU): expert parallel, each rank holds 256/N
-experts and its own ``--tokens`` tokens (weak scaling); token batches are
-all-gathered over NCCL, every rank computes its local experts' partial sums
-for the gathered batch, and a reduce-scatter returns each rank its tokens'
-sums (the reference's all-reduce, architecture.py:791-792, restricted to the
-owner's rows).
+experts and its own ``--tokens`` tokens (weak scaling); each rank routes its
+own tokens, tokens and routing are all-gathered over NCCL, every rank runs its
+local experts on the gathered batch (plus the shared expert on its own rows),
+and a reduce-scatter returns each rank its tokens' sums (the reference's
+all-reduce, architecture.py:791-792, restricted to the owner's rows).
 
 ``--impl reference`` times the reference algorithm on the host cores: the
 numpy oracle port (the reference itself is Python/TileLang and is not
@@ -242,23 +242,26 @@ def step_bytes(indices, T, e0, El, router=True, shared=True):
     return {n1: k1, n2: k2, n3: k3, "experts": n_exp, "pairs": pairs}
 
 
-EP_PHASES = ["own_route_shared", "all_gather", "routed_experts", "reduce_scatter", "add_shared"]
+EP_PHASES = ["route", "all_gather", "experts", "reduce_scatter", "to_bf16"]
 
 
 def ep_step_bytes(idx_g, Tloc, world, e0, El):
     """Per-phase bytes of one expert-parallel step (``wanferenz_b200.ep.ep_forward``)."""
     import numpy as np
 
-    own = step_bytes(np.zeros((Tloc, K_TOP), np.int64) - 1, Tloc, e0, El)
     rt = step_bytes(idx_g, Tloc * world, e0, El, router=False, shared=False)
     names = kernel_names()
+    s13 = 2 * I * D + 2 * (I // 128) * (D // 128)
+    s2 = D * I + (D // 128) * (I // 128)
     tok = 2 * D + 12 * K_TOP
-    return {"own_route_shared": sum(own[k] for k in names),
+    # shared expert on the Tloc own rows: its weights, hidden and output rows
+    shared = s13 + s2 + Tloc * (I * 2 + D * 2 * 2)
+    return {"route": ROUTER_BYTES + Tloc * D * 2 + Tloc * K_TOP * 12,
             "all_gather": (world - 1) * Tloc * tok,            # bytes each rank receives
-            "routed_experts": sum(rt[k] for k in names),
+            "experts": sum(rt[k] for k in names) + shared,
             "reduce_scatter": (world - 1) * Tloc * D * 4,      # bytes each rank receives
-            "add_shared": Tloc * D * (4 + 2 + 2),
-            "experts": rt["experts"], "pairs": rt["pairs"]}
+            "to_bf16": Tloc * D * (4 + 2),
+            "experts_touched": rt["experts"], "pairs": rt["pairs"]}
 
 
 # ---------------------------------------------------------------------------
@@ -282,6 +285,8 @@ def run_gpu(args):
     if world > 1:
         import datetime
 
+        # NCCL's version banner would go to stdout ahead of the result line
+        os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     T = args.tokens
@@ -311,13 +316,12 @@ def run_gpu(args):
         wg = [torch.empty(Tgl, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
         part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]
         mine = [torch.empty(Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
-        sh = [torch.empty(Tloc, D, dtype=torch.bfloat16, device=dev) for _ in range(n)]
         rw = [torch.empty(Tloc, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
         ri = [torch.empty(Tloc, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
         pev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(EP_PHASES) + 1)] for _ in range(n)]
 
         def one_ep(i, timed=False):
-            """Token-owner split (wanferenz_b200.ep.ep_forward) through the C ABI."""
+            """``wanferenz_b200.ep.ep_forward`` through the C ABI."""
             lay = layers[i % len(layers)]
             st = L.stream_ptr()
             cfg, wst, ws, wsn = ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(lay.workspace), \
@@ -325,24 +329,21 @@ def run_gpu(args):
             ev = pev[i] if timed else None
             if ev:
                 ev[0].record()
-            L.check(lib.wf_moe_forward_ep(cfg, wst, L.ptr(xs[i]), None, Tloc, L.WF_EP_SHARED_ONLY, None, None,
-                                          L.ptr(sh[i]), None, L.ptr(rw[i]), L.ptr(ri[i]), ws, wsn, st),
-                    "wf_moe_forward_ep")
+            L.check(lib.wf_moe_route(cfg, wst, L.ptr(xs[i]), None, Tloc, L.ptr(rw[i]), L.ptr(ri[i]), ws, wsn, st),
+                    "wf_moe_route")
             if ev:
                 ev[1].record()
             ep.gather_tokens(xs[i], rw[i], ri[i], xg[i], wg[i], idx[i])
             if ev:
                 ev[2].record()
-            L.check(lib.wf_moe_forward_ep(cfg, wst, L.ptr(xg[i]), None, Tgl, L.WF_EP_ROUTED_ONLY, L.ptr(wg[i]),
-                                          L.ptr(idx[i]), None, L.ptr(part[i]), None, None, ws, wsn, st),
-                    "wf_moe_forward_ep")
+            L.check(lib.wf_moe_forward_ep(cfg, wst, L.ptr(xg[i]), Tgl, L.ptr(wg[i]), L.ptr(idx[i]), rank * Tloc,
+                                          Tloc, L.ptr(part[i]), ws, wsn, st), "wf_moe_forward_ep")
             if ev:
                 ev[3].record()
             dist.reduce_scatter_tensor(mine[i], part[i])
             if ev:
                 ev[4].record()
-            L.check(lib.wf_moe_add_shared(L.ptr(mine[i]), L.ptr(sh[i]), Tloc * D, L.ptr(ys[i]), st),
-                    "wf_moe_add_shared")
+            L.check(lib.wf_moe_to_bf16(L.ptr(mine[i]), Tloc * D, L.ptr(ys[i]), st), "wf_moe_to_bf16")
             if ev:
                 ev[5].record()
 
@@ -390,6 +391,10 @@ def run_gpu(args):
         big = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
         for _ in range(10):
             big.add_(1)
+        if world > 1:
+            # the ranks' queues line up here on the device, so the first timed
+            # collective does not absorb their skew
+            dist.all_reduce(torch.zeros(1, device=dev))
         for i in range(W, n):
             one(i, timed=True)
         torch.cuda.synchronize()
@@ -418,8 +423,7 @@ def run_gpu(args):
             byts = [ep_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
-        layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else
-                                            ["own_route_shared", "routed_experts", "add_shared"]))
+        layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else ["route", "experts", "to_bf16"]))
         hist = [np.bincount(r.ravel(), minlength=E) for r in routing]
         tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
                "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
@@ -477,7 +481,7 @@ def run_gpu(args):
             "us_per_step": round(main["ms"] * 1e3, 2),
             "layer_GBps": round(main["layer_bytes"] / (main["ms"] * 1e-3) / 1e9, 1),
             "kernel_us": {k: round(v * 1e3, 2) for k, v in kms.items()},
-            "experts_touched_per_rank": round(main["bytes"]["experts"], 1),
+            "experts_touched_per_rank": round(main["bytes"]["experts" if world == 1 else "experts_touched"], 1),
             "tokens_per_expert": main["tpe"],
             "sweep": sweep,
         },
@@ -486,9 +490,9 @@ def run_gpu(args):
                      "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
         "clocks": main["clocks"],
-        # single GPU: K1 + two expert phases; multi-GPU: the same three for the own
-        # tokens (router + shared) and for the gathered batch (routed), plus add_shared
-        "gpu_launches": 3 * args.steps if world == 1 else 7 * args.steps,
+        # single GPU: K1 + two expert phases; multi-GPU: the router, the same three
+        # on the gathered batch, and the bf16 cast
+        "gpu_launches": 3 * args.steps if world == 1 else 5 * args.steps,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

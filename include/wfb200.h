@@ -44,10 +44,6 @@ extern "C" {
 #define WF_SCALE_F32 0  /* float32 scales                                   */
 #define WF_SCALE_E8M0 1 /* e8m0 byte scales                                 */
 
-/* modes of wf_moe_forward_ep */
-#define WF_EP_SHARED_ONLY 1 /* route the rank's own tokens, shared expert only */
-#define WF_EP_ROUTED_ONLY 2 /* given routing, local routed experts only        */
-
 /* router score functions: ModelArgs.score_func (architecture.py:59) */
 #define WF_SCORE_SOFTMAX 0
 #define WF_SCORE_SIGMOID 1
@@ -149,29 +145,28 @@ int wf_moe_forward_noalloc(const wf_moe_config *cfg, const wf_moe_weights *w, co
                            const int64_t *input_ids, int32_t T, void *y, float *out_weights,
                            int64_t *out_indices, void *stream);
 
-/* Expert-parallel layer split by token ownership.  The reference (MoE.forward,
- * architecture.py:749-756, 785-794) has every rank route the whole batch, run
- * its local experts and the shared expert on it, and all-reduce; here a rank
- * routes and runs the shared expert for its own tokens only, and the routed
- * experts run on the all-gathered batch with that routing:
- *   mode WF_EP_SHARED_ONLY: x = the rank's own [T, D] tokens; writes the
- *     routing (out_weights, out_indices [T, topk], required) and
- *     y [T, D] bf16 = the shared expert's output;
- *   mode WF_EP_ROUTED_ONLY: x = the gathered [T, D] batch, in_weights /
- *     in_indices [T, topk] its gathered routing; writes y_partial [T, D] f32 =
- *     the ascending-expert sum of the local experts (zero rows for tokens with
- *     none); the caller reduce-scatters it and calls wf_moe_add_shared.
- * The result equals the whole-layer forward's up to the fp32 order of the
- * cross-rank sum.  Both modes use the workspace of wf_moe_workspace_bytes. */
-int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
-                      const int64_t *input_ids, int32_t T, int32_t mode, const float *in_weights,
-                      const int64_t *in_indices, void *y, float *y_partial, float *out_weights,
-                      int64_t *out_indices, void *workspace, size_t workspace_bytes, void *stream);
+/* Expert-parallel forward on a gathered batch with its routing given.  The
+ * reference (MoE.forward, architecture.py:749-756, 785-794) has every rank
+ * route the whole batch, run its local experts and the shared expert on all
+ * of it, and all-reduce.  Here each rank routes only its own tokens
+ * (wf_moe_route), the tokens and their routing are all-gathered, and this call
+ * runs, on the gathered x [T, D] with in_weights / in_indices [T, topk]
+ * (global expert ids):
+ *   - the rank's local experts on every row (ascending expert id), and
+ *   - the shared expert on rows [shared_row0, shared_row0 + shared_rows) only
+ *     (the rank's own tokens; 0 rows for none), added to those rows,
+ * into y_partial [T, D] f32.  Reduce-scattering y_partial over the ranks (each
+ * rank's shared rows are its own) gives each rank routed + shared for its
+ * rows, then wf_moe_to_bf16.  The result equals the whole-layer forward's up to
+ * the fp32 order of the cross-rank sum.  Same workspace as wf_moe_forward. */
+int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x, int32_t T,
+                      const float *in_weights, const int64_t *in_indices, int32_t shared_row0,
+                      int32_t shared_rows, float *y_partial, void *workspace, size_t workspace_bytes,
+                      void *stream);
 
-/* y[i] = bf16(y_partial[i] + shared[i]) for i < n (bf16 shared output of
- * wf_moe_forward_ep, f32 reduced partial): MoE.forward's last step
- * (architecture.py:793-794) in the split of wf_moe_forward_ep. */
-int wf_moe_add_shared(const float *y_partial, const void *shared, int64_t n, void *y, void *stream);
+/* dst[i] = bf16(src[i]) for i < n (round to nearest even): the last step of
+ * MoE.forward's output (architecture.py:794) after the cross-rank sum. */
+int wf_moe_to_bf16(const float *src, int64_t n, void *dst, void *stream);
 
 /* Expert-parallel epilogue: y[t] = bf16(y_partial_reduced[t] + shared_out[row0 + t])
  * for t < T, where shared_out is the shared expert's output that the last

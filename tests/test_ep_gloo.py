@@ -1,11 +1,11 @@
 """Expert-parallel host logic on 2 CPU ranks (gloo).
 
-``wanferenz_b200.ep.ep_forward`` (route + shared expert of the owned tokens,
-all-gather tokens and routing, local-expert partials with the given routing,
-reduce-scatter, add the shared rows) is driven with a CPU stand-in layer whose
-parts come from the oracle (architecture.py:749-756, 785-794).  The result must
-equal the single-process oracle up to the fp32 summation order of the partials
-(the shared expert's output is bf16 in the reference already, 121-134).
+``wanferenz_b200.ep.ep_forward`` (route the owned tokens, all-gather tokens
+and routing, local experts on the gathered batch with the given routing plus
+the shared expert on the rank's own rows, reduce-scatter, bf16) is driven with
+a CPU stand-in layer whose parts come from the oracle (architecture.py:749-756,
+785-794).  The result must equal the single-process oracle up to the fp32
+summation order of the partials.
 """
 
 import os
@@ -24,30 +24,28 @@ SPEC = F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="sigmoid", route_scale
 
 
 class OracleShard:
-    """CPU stand-in with MoELayer's route_shared / forward_routed / add_shared contract."""
+    """CPU stand-in with MoELayer's route / forward_ep / to_bf16 contract."""
 
     def __init__(self, syn, lo, hi):
         self.syn, self.lo, self.hi = syn, lo, hi
 
-    def route_shared(self, x, input_ids=None):
-        xf = x.float().numpy()
+    def route(self, x, input_ids=None):
         p = self.syn.params()
-        w, idx, _ = O.gate(xf, p["gate_w"], p.get("gate_b"), p["topk"], p["score_func"],
+        w, idx, _ = O.gate(x.float().numpy(), p["gate_w"], p.get("gate_b"), p["topk"], p["score_func"],
                            p["route_scale"], p.get("tid2eid"), input_ids)
-        sh = O.expert_fp8(xf, *self.syn.shared(), weights=None,
-                          swiglu_limit=SPEC.swiglu_limit, ue8m0=SPEC.ue8m0)
-        shared = torch.from_numpy(O.round_bf16(sh.astype(np.float32))).to(torch.bfloat16)
-        return shared, torch.from_numpy(w), torch.from_numpy(idx)
+        return torch.from_numpy(w), torch.from_numpy(idx)
 
-    def forward_routed(self, x, weights, indices):
+    def forward_ep(self, x, weights, indices, shared_rows=(0, 0)):
         xf = x.float().numpy()
         p, _, _ = O.moe_forward(xf, self.syn.params(), None, expert_range=(self.lo, self.hi),
                                 return_partial=True, routing=(weights.numpy(), indices.numpy()))
-        return torch.from_numpy(p)
+        r0, n = shared_rows
+        p[r0:r0 + n] += O.expert_fp8(xf[r0:r0 + n], *self.syn.shared(), weights=None,
+                                     swiglu_limit=SPEC.swiglu_limit, ue8m0=SPEC.ue8m0)
+        return torch.from_numpy(p.astype(np.float32))
 
-    def add_shared(self, y_partial, shared):
-        y = y_partial.numpy() + shared.float().numpy()
-        return torch.from_numpy(O.round_bf16(y.astype(np.float32))).to(torch.bfloat16)
+    def to_bf16(self, y):
+        return torch.from_numpy(O.round_bf16(y.numpy().astype(np.float32))).to(torch.bfloat16)
 
 
 def _free_port():

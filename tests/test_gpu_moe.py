@@ -178,12 +178,12 @@ def test_expert_parallel_partials_match_oracle():
 
 @pytest.mark.parametrize("T", [1, 5, 16])
 def test_token_owner_split_matches_oracle(T, engine):
-    """The expert-parallel split of ``ep_forward`` with two ranks emulated on one GPU.
+    """The expert-parallel forward of ``ep_forward`` with two ranks emulated on one GPU.
 
-    Each rank routes its own T tokens and runs the shared expert on them
-    (WF_EP_SHARED_ONLY); the gathered 2T tokens and their routing go through
-    each expert shard (WF_EP_ROUTED_ONLY); a rank's rows of the summed partials
-    plus its shared rows must equal the single-layer oracle (architecture.py:777-794).
+    Each rank routes its own T tokens (wf_moe_route); each expert shard runs on
+    the gathered 2T tokens with that routing and the shared expert on its own
+    rank's rows (wf_moe_forward_ep); a rank's rows of the summed partials, cast
+    to bf16, must equal the single-layer oracle (architecture.py:777-794).
     """
     spec = F.LayerSpec(D=512, I=256, E=16, topk=4, score_func="sqrtsoftplus", route_scale=1.5,
                        swiglu_limit=10.0, seed=43)
@@ -197,54 +197,72 @@ def test_token_owner_split_matches_oracle(T, engine):
               U.device_layer(syn, touched, expert_range=(8, 16))]
     xt = U.bf16_tensor(x16)
     idt = torch.from_numpy(ids).cuda()
-    own = [shards[r].route_shared(xt[r * T:(r + 1) * T], idt[r * T:(r + 1) * T]) for r in range(2)]
-    wg = torch.cat([o[1] for o in own])
-    ig = torch.cat([o[2] for o in own])
-    parts = [d.forward_routed(xt, wg, ig) for d in shards]
-    ysum = parts[0] + parts[1]
-    y = torch.cat([shards[r].add_shared(ysum[r * T:(r + 1) * T], own[r][0]) for r in range(2)])
+    own = [shards[r].route(xt[r * T:(r + 1) * T], idt[r * T:(r + 1) * T]) for r in range(2)]
+    wg = torch.cat([o[0] for o in own])
+    ig = torch.cat([o[1] for o in own])
+    parts = [d.forward_ep(xt, wg, ig, shared_rows=(r * T, T)) for r, d in enumerate(shards)]
+    y = shards[0].to_bf16(parts[0] + parts[1])
     torch.cuda.synchronize()
     for d in shards:
         d.read_error()
     tie = U.near_tie_rows(x, syn)
     np.testing.assert_array_equal(ig.cpu().numpy()[~tie], i_ref[~tie])
     np.testing.assert_allclose(wg.cpu().numpy()[~tie], w_ref[~tie], rtol=2e-6, atol=1e-7)
-    sh_ref = O.expert_fp8(x, *syn.shared(), weights=None, swiglu_limit=spec.swiglu_limit, ue8m0=spec.ue8m0)
-    U.assert_layer_close(U.to_f32(torch.cat([o[0] for o in own])), sh_ref, "shared")
     U.assert_layer_close_envelope(U.to_f32(y)[~tie], y_ref[~tie], y_ref32[~tie], f"split T={T}")
-    # the routed-only pass takes the routing it is given: the oracle's, on every row
+    # the given routing is used as is: the oracle's, on every row; shared rows of this shard only
     p0, _, _ = O.moe_forward(x, syn.params(), None, expert_range=(0, 8), return_partial=True,
                              routing=(w_ref, i_ref))
-    q0 = shards[0].forward_routed(xt, torch.from_numpy(w_ref).cuda(), torch.from_numpy(i_ref).cuda())
+    sh = O.expert_fp8(x[:T], *syn.shared(), weights=None, swiglu_limit=spec.swiglu_limit, ue8m0=spec.ue8m0)
+    p0[:T] += sh
+    q0 = shards[0].forward_ep(xt, torch.from_numpy(w_ref).cuda(), torch.from_numpy(i_ref).cuda(), (0, T))
     np.testing.assert_allclose(q0.cpu().numpy(), p0, rtol=1e-2, atol=2e-3)
 
 
-def test_routed_only_rejects_out_of_range_expert():
+def test_forward_ep_rejects_out_of_range_expert():
     spec = F.LayerSpec(D=256, I=128, E=16, topk=2, score_func="sigmoid", route_scale=1.0, seed=44)
     syn = _syn(spec)
     x16, _ = syn.activations(3)
     d = U.device_layer(syn, [], expert_range=(0, 8))
     w = torch.full((3, 2), 0.5, device="cuda")
     idx = torch.tensor([[0, 1], [2, 16], [3, 4]], dtype=torch.int64, device="cuda")
-    d.forward_routed(U.bf16_tensor(x16), w, idx)
+    d.forward_ep(U.bf16_tensor(x16), w, idx)
     with pytest.raises(Exception):
         d.read_error()
     ok = torch.tensor([[0, 9], [2, 15], [3, 4]], dtype=torch.int64, device="cuda")
-    d.forward_routed(U.bf16_tensor(x16), w, ok)
+    d.forward_ep(U.bf16_tensor(x16), w, ok)
     d.read_error()
 
 
-def test_routed_only_shard_without_tokens_gives_zero_partial(engine):
+@pytest.mark.parametrize("shared_rows", [(0, 0), (1, 2)])
+def test_forward_ep_shard_without_tokens(shared_rows, engine):
+    """A shard none of whose experts is routed to: zero rows, plus the shared
+    expert's rows when the window holds any."""
     spec = F.LayerSpec(D=256, I=128, E=16, topk=2, score_func="sigmoid", route_scale=1.0, seed=45)
     syn = _syn(spec)
     x16, _ = syn.activations(4)
     d = U.device_layer(syn, [], expert_range=(8, 16))
     w = torch.rand(4, 2, device="cuda")
     idx = torch.tensor([[0, 1], [2, 3], [7, 4], [5, 6]], dtype=torch.int64, device="cuda")
-    q = d.forward_routed(U.bf16_tensor(x16), w, idx)
+    q = d.forward_ep(U.bf16_tensor(x16), w, idx, shared_rows)
     torch.cuda.synchronize()
     d.read_error()
-    assert torch.count_nonzero(q).item() == 0
+    r0, n = shared_rows
+    rest = torch.cat([q[:r0], q[r0 + n:]])
+    assert torch.count_nonzero(rest).item() == 0
+    if n:
+        sh = O.expert_fp8(O.bf16_to_f32(x16)[r0:r0 + n], *syn.shared(), weights=None,
+                          swiglu_limit=spec.swiglu_limit, ue8m0=spec.ue8m0)
+        U.assert_layer_close(q[r0:r0 + n].cpu().numpy(), sh, "shared rows")
+
+
+def test_to_bf16_rounds_to_nearest_even():
+    from wanferenz_b200 import _lib as L
+
+    lib = L.load()
+    v = torch.tensor([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, 3.4e38, 1e-40], device="cuda")
+    out = torch.empty(6, dtype=torch.bfloat16, device="cuda")
+    L.check(lib.wf_moe_to_bf16(L.ptr(v), 6, L.ptr(out), L.stream_ptr()), "wf_moe_to_bf16")
+    assert torch.equal(out, v.to(torch.bfloat16))
 
 
 def test_shard_without_tokens_gives_zero_partial():

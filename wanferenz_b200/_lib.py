@@ -15,7 +15,6 @@ WF_OK = 0
 WF_E_SHAPE, WF_E_DTYPE, WF_E_EXPERT_ID, WF_E_TIMEOUT, WF_E_CUDA, WF_E_RANGE, WF_E_ARG = (
     -1, -2, -3, -4, -5, -6, -7)
 WF_SCALE_F32, WF_SCALE_E8M0 = 0, 1
-WF_EP_SHARED_ONLY, WF_EP_ROUTED_ONLY = 1, 2  # wf_moe_forward_ep modes
 WF_SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 
 # every symbol include/wfb200.h declares
@@ -24,7 +23,7 @@ EXPORTS = (
     "wf_moe_forward_timed",
     "wf_moe_finish", "wf_moe_route", "wf_moe_read_error", "wf_act_quant", "wf_fp4_act_quant",
     "wf_fp8_gemm", "wf_fp4_gemm", "wf_grouped_fp4_gemm", "wf_gemm_workspace_bytes",
-    "wf_fp4_scales_in_range", "wf_moe_forward_noalloc", "wf_moe_forward_ep", "wf_moe_add_shared",
+    "wf_fp4_scales_in_range", "wf_moe_forward_noalloc", "wf_moe_forward_ep", "wf_moe_to_bf16",
 )
 
 
@@ -72,9 +71,9 @@ def _declare(lib):
                                                 P, P, I32, P, P, P, P, P, SZ, P,
                                                 ctypes.POINTER(ctypes.c_void_p)]),
         "wf_moe_finish": (ctypes.c_int, [ctypes.POINTER(MoeConfig), P, I32, I32, P, P, SZ, P]),
-        "wf_moe_forward_ep": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, P,
-                                             I32, I32, P, P, P, P, P, P, P, SZ, P]),
-        "wf_moe_add_shared": (ctypes.c_int, [P, P, I64, P, P]),
+        "wf_moe_forward_ep": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, I32,
+                                             P, P, I32, I32, P, P, SZ, P]),
+        "wf_moe_to_bf16": (ctypes.c_int, [P, I64, P, P]),
         "wf_moe_route": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, P,
                                         I32, P, P, P, SZ, P]),
         "wf_moe_read_error": (ctypes.c_int, [P, SZ, P]),

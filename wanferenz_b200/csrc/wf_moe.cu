@@ -107,11 +107,14 @@ struct MoeArgs {
     Geo g;
     int tc;              // expert phases on tcgen05 (k_moe_tc): K1 quantizes x, skips the shared expert
     uint8_t *xq, *xs;    // E4M3 tokens [T, D] and their e8m0 scales [T, D/128] (tc)
-    // expert-parallel split (wf_moe_forward_ep): 0 whole layer; WF_EP_SHARED_ONLY route
-    // and shared expert only; WF_EP_ROUTED_ONLY given routing, local routed experts only
-    int ep_mode;
-    const float *in_w;         // [T, topk] given routing weights (routed-only)
-    const long long *in_idx;   // [T, topk] given expert indices (routed-only)
+    // routing given by the caller (wf_moe_forward_ep): no router, in_w / in_idx instead
+    int given;
+    const float *in_w;         // [T, topk] routing weights
+    const long long *in_idx;   // [T, topk] global expert ids
+    // the shared expert runs on rows [sh0, sh0 + shT); sh_add: the combine adds those
+    // rows to the output (whole layer: all rows; partial forward: none, wf_moe_finish
+    // adds them; expert-parallel: the rank's own rows of the gathered batch)
+    int sh0, shT, sh_add;
 };
 
 // Dense GEMM (operator entry points) arguments.
@@ -164,7 +167,7 @@ __device__ __forceinline__ Item decode_moe(int kid, const MoeArgs &a, int i, int
         it.grow[0] = hb * nh; it.grow[1] = I + hb * nh;
         it.wsrc[0] = a.sw13 + (size_t)it.grow[0] * D;
         it.wsrc[1] = a.sw13 + (size_t)it.grow[1] * D;
-        it.row0 = hb * nh; it.a = 0; it.tok0 = tg * TPI; it.ntok = min(TPI, a.T - tg * TPI);
+        it.row0 = hb * nh; it.a = 0; it.tok0 = a.sh0 + tg * TPI; it.ntok = min(TPI, a.shT - tg * TPI);
         return it;
     }
     if (kid == KID_MID && i >= n_it2) {  // shared expert w2
@@ -175,7 +178,7 @@ __device__ __forceinline__ Item decode_moe(int kid, const MoeArgs &a, int i, int
         it.grow[0] = rb * nr;
         it.wsrc[0] = a.sw2 + (size_t)it.grow[0] * I;
         it.wsrc[1] = it.wsrc[0];
-        it.row0 = rb * nr; it.a = 0; it.tok0 = tg * TPI; it.ntok = min(TPI, a.T - tg * TPI);
+        it.row0 = rb * nr; it.a = 0; it.tok0 = a.sh0 + tg * TPI; it.ntok = min(TPI, a.shT - tg * TPI);
         return it;
     }
     // routed items (tables in shared memory)
@@ -952,7 +955,7 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
     const int TW = (T + 31) >> 5;
     // ---- 1. top-k: one warp per token, scores of the warp's token in shared memory
     // (routed-only calls take the routing computed by the ranks that own the tokens)
-    if (a.ep_mode == WF_EP_ROUTED_ONLY) {
+    if (a.given) {
         for (int slot = tid; slot < T * K; slot += NCT) {
             long long e = __ldg(a.in_idx + slot);
             if (e < 0 || e >= E) { atomicOr(a.err, kErrExpertId); e = 0; }
@@ -969,16 +972,6 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
     }
     bar_sync(1, NCT);
     if (a.route_only) {
-        __threadfence();
-        return;
-    }
-    if (a.ep_mode == WF_EP_SHARED_ONLY) {
-        // no routed work: empty dispatch tables, so only the shared expert runs
-        if (tid == 0) {
-            a.act_off[0] = 0; a.act_it2[0] = 0; a.act_it3[0] = 0;
-            a.hdr[H_NACT] = 0; a.hdr[H_IT2] = 0; a.hdr[H_IT3] = 0; a.hdr[H_TGT] = 0; a.hdr[H_NPAIR] = 0;
-        }
-        for (int t = tid; t < T; t += NCT) a.tok_np[t] = 0;
         __threadfence();
         return;
     }
@@ -1083,12 +1076,9 @@ __device__ void combine_rows(const MoeArgs &a, int row0, int nrows) {
             const int p = __ldcg(a.tok_pairs + t * K + qq);
             acc += bf16_bits_to_f32(__ldcg(o + (size_t)p * D + r));
         }
-        if (a.partial) {
-            a.y_partial[(size_t)t * D + r] = acc;
-        } else {
-            acc += bf16_bits_to_f32(__ldcg(os + (size_t)t * D + r));
-            a.y[(size_t)t * D + r] = __float2bfloat16_rn(acc);
-        }
+        if (a.sh_add && t >= a.sh0 && t < a.sh0 + a.shT) acc += bf16_bits_to_f32(__ldcg(os + (size_t)t * D + r));
+        if (a.partial) a.y_partial[(size_t)t * D + r] = acc;
+        else a.y[(size_t)t * D + r] = __float2bfloat16_rn(acc);
     }
 }
 
@@ -1128,7 +1118,9 @@ __device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows, const uin
         uint4 sv[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
-            sv[j] = (!a.partial && base + j * NTH < n) ? ldcg128(a.os + (size_t)tt[j] * D + rr[j]) : make_uint4(0, 0, 0, 0);
+            sv[j] = (a.sh_add && base + j * NTH < n && tt[j] >= a.sh0 && tt[j] < a.sh0 + a.shT)
+                        ? ldcg128(a.os + (size_t)tt[j] * D + rr[j])
+                        : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             if (base + j * NTH >= n) continue;
@@ -1147,6 +1139,14 @@ __device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows, const uin
             }
             const int t = tt[j], r = rr[j];
             if (a.partial) {
+                if (a.sh_add && t >= a.sh0 && t < a.sh0 + a.shT) {
+                    const uint32_t u[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[2 * e] += bf16_bits_to_f32(u[e] & 0xffffu);
+                        acc[2 * e + 1] += bf16_bits_to_f32(u[e] >> 16);
+                    }
+                }
                 float4 *dst = reinterpret_cast<float4 *>(a.y_partial + (size_t)t * D + r);
                 dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
                 dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
@@ -1242,8 +1242,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     init_smem(sm);
     pdl_wait();
     pdl_launch_dependents();
-    const bool given = a.ep_mode == WF_EP_ROUTED_ONLY;
-    const int n = (a.route_only || a.tc || given) ? 0 : (a.I / a.g.nhs13) * cdiv(a.T, TPI);
+    const bool given = a.given;
+    const int n = (a.route_only || a.tc) ? 0 : (a.I / a.g.nhs13) * cdiv(a.shT, TPI);
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_moe(KID_UP, a, i, 0, 0, nullptr, nullptr, nullptr); };
@@ -1324,7 +1324,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
     const int n_act = a.hdr[H_NACT], n_it2 = a.hdr[H_IT2];
     load_route(sm, a.act_expert, a.act_off, a.act_it2, a.pair_tok, a.pair_w, n_act, a.hdr[H_NPAIR]);
     const RouteSm rt = route_sm(sm);
-    const int n = n_it2 + (a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : (a.D / a.g.rs2) * cdiv(a.T, TPI));
+    const int n = n_it2 + (a.D / a.g.rs2) * cdiv(a.shT, TPI);
     int i0, i1;
     item_range(n, i0, i1);
     auto decode = [&, c = Cursor{-1, 0}](int i) mutable {
@@ -1420,6 +1420,11 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ Mo
 __global__ void k_moe_finish(const float *yp, const __nv_bfloat16 *os, __nv_bfloat16 *y, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         y[i] = __float2bfloat16_rn(yp[i] + __bfloat162float(os[i]));
+}
+
+__global__ void k_to_bf16(const float *src, __nv_bfloat16 *dst, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
 }
 
 #include "wf_moe_tc.cuh"
@@ -1860,7 +1865,7 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
 
 int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
               const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a,
-              wf::mtc::TcArgs *t = nullptr) {
+              wf::mtc::TcArgs *t = nullptr, bool routing_given = false) {
     int rc = check_cfg(c);
     if (rc) return rc;
     if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
@@ -1868,8 +1873,10 @@ int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
     const WsLayout L = ws_layout(c);
     if (ws_bytes < L.total) return fail(WF_E_ARG, "workspace too small");
     if (!w->gate_w) return fail(WF_E_ARG, "null gate weight");
-    if (c->hash_layer && (!w->tid2eid || !ids)) return fail(WF_E_ARG, "hash layer needs tid2eid and input_ids");
+    if (c->hash_layer && !routing_given && (!w->tid2eid || !ids))
+        return fail(WF_E_ARG, "hash layer needs tid2eid and input_ids");
     memset(&a, 0, sizeof(a));
+    a.sh0 = 0; a.shT = T; a.sh_add = 1;  // the shared expert on every row, added by the combine
     a.T = T; a.D = c->dim; a.I = c->inter_dim; a.E = c->n_experts; a.El = c->n_local_experts;
     a.e0 = c->expert_offset; a.topk = c->topk; a.score_func = c->score_func;
     a.hash = c->hash_layer; a.ue8m0 = c->ue8m0; a.vocab = c->vocab;
@@ -1989,6 +1996,7 @@ int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
+    a.sh_add = !a.partial;  // a partial forward leaves the shared rows to wf_moe_finish
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
     return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
 }
@@ -2008,42 +2016,40 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
+    a.sh_add = !a.partial;  // a partial forward leaves the shared rows to wf_moe_finish
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
     return launch_moe(a, false, (cudaStream_t)stream, events, &t);
 }
 
-int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
-                      const int64_t *input_ids, int32_t T, int32_t mode, const float *in_weights,
-                      const int64_t *in_indices, void *y, float *y_partial, float *out_weights,
-                      int64_t *out_indices, void *workspace, size_t workspace_bytes, void *stream) {
-    if (mode != WF_EP_SHARED_ONLY && mode != WF_EP_ROUTED_ONLY) return fail(WF_E_ARG, "bad expert-parallel mode");
+int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x, int32_t T,
+                      const float *in_weights, const int64_t *in_indices, int32_t shared_row0,
+                      int32_t shared_rows, float *y_partial, void *workspace, size_t workspace_bytes,
+                      void *stream) {
     int rc = check_expert_ptrs(w);
     if (rc) return rc;
+    if (!in_weights || !in_indices || !y_partial) return fail(WF_E_ARG, "null routing or output");
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
-    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
+    rc = fill_args(cfg, w, x, nullptr, T, workspace, workspace_bytes, a, &t, true);
     if (rc) return rc;
-    a.ep_mode = mode;
-    if (mode == WF_EP_SHARED_ONLY) {
-        if (!y || !out_weights || !out_indices) return fail(WF_E_ARG, "shared-only mode needs y and the routing outputs");
-        a.y = (__nv_bfloat16 *)y; a.y_partial = nullptr; a.partial = 0;
-        a.out_w = out_weights; a.out_idx = (long long *)out_indices;
-    } else {
-        if (!y_partial || !in_weights || !in_indices) return fail(WF_E_ARG, "routed-only mode needs y_partial and the routing");
-        a.y = nullptr; a.y_partial = y_partial; a.partial = 1;
-        a.in_w = in_weights; a.in_idx = (const long long *)in_indices;
-        a.out_w = nullptr; a.out_idx = nullptr;
-    }
+    if (shared_row0 < 0 || shared_rows < 0 || shared_row0 + shared_rows > T)
+        return fail(WF_E_SHAPE, "shared rows outside 0..T");
+    a.given = 1;
+    a.in_w = in_weights; a.in_idx = (const long long *)in_indices;
+    a.sh0 = shared_row0; a.shT = shared_rows; a.sh_add = 1;
+    a.y = nullptr; a.y_partial = y_partial; a.partial = 1;
+    a.out_w = nullptr; a.out_idx = nullptr;
     return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
 }
 
-int wf_moe_add_shared(const float *y_partial, const void *shared, int64_t n, void *y, void *stream) {
-    if (!y_partial || !shared || !y) return fail(WF_E_ARG, "null pointer");
+int wf_moe_to_bf16(const float *src, int64_t n, void *dst, void *stream) {
+    if (!src || !dst) return fail(WF_E_ARG, "null pointer");
     if (n <= 0 || n > (int64_t)1 << 30) return fail(WF_E_SHAPE, "n outside 1..2^30");
-    wf::k_moe_finish<<<(unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, (cudaStream_t)stream>>>(
-        y_partial, (const __nv_bfloat16 *)shared, (__nv_bfloat16 *)y, (int)n);
+    const int64_t blocks = (n + 255) / 256;
+    wf::k_to_bf16<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, (cudaStream_t)stream>>>(
+        src, (__nv_bfloat16 *)dst, (int)n);
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? WF_OK : cuda_fail(e, "add_shared launch");
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "to_bf16 launch");
 }
 
 int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,

@@ -128,7 +128,7 @@ __device__ __forceinline__ TItem decode(const MoeArgs &a, const TRoute &r, TCurs
     if (i < r.ns) {
         const int tg = i / r.nblk;
         it.shared = 1; it.el = 0; it.blk = i - tg * r.nblk;
-        it.tok0 = tg * NT; it.ntok = min(NT, a.T - it.tok0);
+        it.tok0 = a.sh0 + tg * NT; it.ntok = min(NT, a.shT - tg * NT);
     } else {
         const int j = i - r.ns;
         if (!c.init) {
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         r.act_it = rt_s + 2 * (MAX_E + 1);
         r.n_act = n_act;
         r.nblk = PH == 2 ? a.I / 128 : a.D / 256;
-        r.ns = a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : r.nblk * cdiv(a.T, NT);  // shared items
+        r.ns = r.nblk * cdiv(a.shT, NT);  // shared items
         if (PH == 3) {
             // the combine's pair lists (written by the router kernel)
             for (int k = threadIdx.x; k < a.T * a.topk; k += THREADS) tp_s[k] = (int16_t)__ldcg(a.tok_pairs + k);
@@ -540,7 +540,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 bar_sync(1, NWK);
                 if (tid == 0) {
                     const unsigned target =
-                        (unsigned)(a.hdr[H_TGT] + (a.ep_mode == WF_EP_ROUTED_ONLY ? 0 : cdiv(a.T, NT)));
+                        (unsigned)(a.hdr[H_TGT] + cdiv(a.shT, NT));
                     const unsigned old = atomicAdd(a.cnt_rb + it.blk, 1u);
                     *flag = old == target - 1;
                 }

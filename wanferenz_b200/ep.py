@@ -3,18 +3,17 @@
 Rank ``r`` of ``P`` holds experts ``[r*E/P, (r+1)*E/P)`` (architecture.py:749-756)
 and its own batch of ``T`` tokens (decode serving with data-parallel tokens).
 The reference all-reduces a layer that every rank computes for the whole
-batch; here the work splits by who owns what:
+batch; here each token is routed once, on the rank that owns it:
 
-1. each rank routes its own ``T`` tokens and runs the shared expert on them
-   (``MoELayer.route_shared``: one router pass per token in the job, not one
-   per rank);
-2. all-gather the ``P*T`` tokens and their routing (NCCL over NVLink);
-3. every rank runs its local experts on the gathered batch with that routing
-   (``MoELayer.forward_routed``) -> fp32 partial sums ``[P*T, D]``;
-4. reduce-scatter the partials, so each rank receives the sum over ranks for
-   its own rows (the reference's ``dist.all_reduce(y)``, architecture.py:791-792,
-   restricted to the rows the rank owns);
-5. add the shared expert's rows and cast to bf16 (793-794).
+1. route the rank's own ``T`` tokens (``MoELayer.route``);
+2. all-gather the ``P*T`` tokens and their routing (one NCCL group);
+3. one forward on the gathered batch with that routing: the rank's local
+   experts on every row, the shared expert on the rank's own rows only
+   (``MoELayer.forward_ep``) -> fp32 partial sums ``[P*T, D]``;
+4. reduce-scatter: each rank receives the sum over ranks for its own rows
+   (the reference's ``dist.all_reduce(y)``, architecture.py:791-792,
+   restricted to those rows), shared expert included (793);
+5. cast to bf16 (794).
 """
 
 from __future__ import annotations
@@ -42,17 +41,18 @@ def gather_tokens(x, w, idx, xg, wg, ig, group=None):
 def ep_forward(layer, x, input_ids=None, group=None):
     """One expert-parallel MoE forward of this rank's ``x [T, D]`` (T equal on all ranks)."""
     world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
     T = x.size(0)
     x = x.contiguous()
-    shared, w, idx = layer.route_shared(x, input_ids)
+    w, idx = layer.route(x, input_ids)
     xg = torch.empty(world * T, x.size(1), dtype=x.dtype, device=x.device)
     wg = torch.empty(world * T, w.size(1), dtype=w.dtype, device=x.device)
     ig = torch.empty(world * T, idx.size(1), dtype=idx.dtype, device=x.device)
     gather_tokens(x, w.contiguous(), idx.contiguous(), xg, wg, ig, group)
-    part = layer.forward_routed(xg, wg, ig)
+    part = layer.forward_ep(xg, wg, ig, shared_rows=(rank * T, T))
     mine = torch.empty(T, x.size(1), dtype=torch.float32, device=x.device)
     dist.reduce_scatter_tensor(mine, part, group=group)
-    return layer.add_shared(mine, shared)
+    return layer.to_bf16(mine)
 
 
 def shard_range(n_experts, world, rank):

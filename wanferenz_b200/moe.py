@@ -185,49 +185,31 @@ class MoELayer:
     # ------------------------------------------------------------------------
     # expert-parallel split by token ownership (wanferenz_b200.ep)
     # ------------------------------------------------------------------------
-    def route_shared(self, x, input_ids=None):
-        """Routes this rank's own tokens and runs the shared expert on them.
-
-        Returns ``(shared_out [T, D] bf16, weights [T, k] f32, indices [T, k] int64)``
-        (``wf_moe_forward_ep`` mode WF_EP_SHARED_ONLY)."""
+    def forward_ep(self, x, weights, indices, shared_rows=(0, 0), out=None):
+        """Local experts on a gathered batch ``x [T, D]`` with its given routing
+        (``weights [T, k]``, global ``indices [T, k]``), plus the shared expert on
+        rows ``[r0, r0 + n)`` = ``shared_rows``: the fp32 partial ``[T, D]`` to be
+        summed over ranks (``wf_moe_forward_ep``)."""
         x = x.contiguous()
         T = x.size(0)
         if T > self.max_tokens:
-            raise WfUnsupported("route_shared: T exceeds max_tokens")
-        if input_ids is not None:
-            input_ids = input_ids.reshape(-1).to(torch.int64).contiguous()
-        ys = torch.empty(T, self.dim, dtype=torch.bfloat16, device=x.device)
-        rw = torch.empty(T, self.topk, dtype=torch.float32, device=x.device)
-        ri = torch.empty(T, self.topk, dtype=torch.int64, device=x.device)
-        L.check(self.lib.wf_moe_forward_ep(ctypes.byref(self.cfg), ctypes.byref(self.wstruct), L.ptr(x),
-                                           L.ptr(input_ids), T, L.WF_EP_SHARED_ONLY, None, None, L.ptr(ys),
-                                           None, L.ptr(rw), L.ptr(ri), L.ptr(self.workspace),
-                                           self.workspace.numel(), L.stream_ptr()), "wf_moe_forward_ep")
-        return ys, rw, ri
-
-    def forward_routed(self, x, weights, indices, out=None):
-        """Local routed experts on a gathered batch with its given routing: the fp32
-        ascending-expert partial sum ``[T, D]`` (mode WF_EP_ROUTED_ONLY)."""
-        x = x.contiguous()
-        T = x.size(0)
-        if T > self.max_tokens:
-            raise WfUnsupported("forward_routed: T exceeds max_tokens")
+            raise WfUnsupported("forward_ep: T exceeds max_tokens")
         weights = weights.to(torch.float32).contiguous()
         indices = indices.to(torch.int64).contiguous()
         yp = out if out is not None else torch.empty(T, self.dim, dtype=torch.float32, device=x.device)
-        L.check(self.lib.wf_moe_forward_ep(ctypes.byref(self.cfg), ctypes.byref(self.wstruct), L.ptr(x),
-                                           None, T, L.WF_EP_ROUTED_ONLY, L.ptr(weights), L.ptr(indices),
-                                           None, L.ptr(yp), None, None, L.ptr(self.workspace),
-                                           self.workspace.numel(), L.stream_ptr()), "wf_moe_forward_ep")
+        r0, n = shared_rows
+        L.check(self.lib.wf_moe_forward_ep(ctypes.byref(self.cfg), ctypes.byref(self.wstruct), L.ptr(x), T,
+                                           L.ptr(weights), L.ptr(indices), int(r0), int(n), L.ptr(yp),
+                                           L.ptr(self.workspace), self.workspace.numel(), L.stream_ptr()),
+                "wf_moe_forward_ep")
         return yp
 
-    def add_shared(self, y_partial, shared_out, out=None):
-        """``bf16(y_partial + shared_out)`` (architecture.py:793-794)."""
-        y = out if out is not None else torch.empty(shared_out.shape, dtype=torch.bfloat16,
-                                                    device=shared_out.device)
-        L.check(self.lib.wf_moe_add_shared(L.ptr(y_partial.contiguous()), L.ptr(shared_out.contiguous()),
-                                           y_partial.numel(), L.ptr(y), L.stream_ptr()), "wf_moe_add_shared")
-        return y
+    def to_bf16(self, y, out=None):
+        """``bf16(y)`` of an fp32 ``y`` (``wf_moe_to_bf16``)."""
+        y = y.contiguous()
+        o = out if out is not None else torch.empty(y.shape, dtype=torch.bfloat16, device=y.device)
+        L.check(self.lib.wf_moe_to_bf16(L.ptr(y), y.numel(), L.ptr(o), L.stream_ptr()), "wf_moe_to_bf16")
+        return o
 
     def route(self, x, input_ids=None):
         """``Gate.forward`` (architecture.py:696-718): ``(weights [T,k] f32, indices [T,k] int64)``."""
