@@ -209,7 +209,7 @@ def kernel_names():
 
 # ncu traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the tcgen05
 # expert phases, 16 tokens, uniform routing: profiles/k_moe_tc_config2_T16.md
-MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 759.0e6, "k_moe_tc<3>": 389.6e6}
+MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 763.3e6, "k_moe_tc<3>": 387.5e6}
 
 
 def step_bytes(indices, T, e0, El, router=True, shared=True):
