@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--routing", default="uniform", choices=("uniform", "zipf"),
                     help="zipf: BASELINE config 4 popularity, gate bias += beta*log(rank^-1.2)")
     ap.add_argument("--zipf-beta", type=float, default=0.06)
+    ap.add_argument("--combine", default="reduce_scatter", choices=("reduce_scatter", "all_to_all"),
+                    help="N > 1: NCCL reduce-scatter of the partials, or all-to-all + ascending-rank sum")
     ap.add_argument("--init", default="quant", choices=("quant", "random"),
                     help="quant: N(0,0.02) weights through the FP4 quantizer; random: random FP4 bytes "
                          "with typical scales (fewer launches, for profiler captures)")
@@ -242,10 +244,10 @@ def step_bytes(indices, T, e0, El, router=True, shared=True):
     return {n1: k1, n2: k2, n3: k3, "experts": n_exp, "pairs": pairs}
 
 
-EP_PHASES = ["route", "all_gather", "experts", "reduce_scatter", "to_bf16"]
+EP_PHASES = ["route", "all_gather", "experts", "combine", "to_bf16"]
 
 
-def ep_step_bytes(idx_g, Tloc, world, e0, El):
+def ep_step_bytes(idx_g, Tloc, world, e0, El, combine="reduce_scatter"):
     """Per-phase bytes of one expert-parallel step (``wanferenz_b200.ep.ep_forward``)."""
     import numpy as np
 
@@ -259,8 +261,8 @@ def ep_step_bytes(idx_g, Tloc, world, e0, El):
     return {"route": ROUTER_BYTES + Tloc * D * 2 + Tloc * K_TOP * 12,
             "all_gather": (world - 1) * Tloc * tok,            # bytes each rank receives
             "experts": sum(rt[k] for k in names) + shared,
-            "reduce_scatter": (world - 1) * Tloc * D * 4,      # bytes each rank receives
-            "to_bf16": Tloc * D * (4 + 2),
+            "combine": (world - 1) * Tloc * D * 4,             # bytes each rank receives
+            "to_bf16": Tloc * D * ((4 * world if combine == "all_to_all" else 4) + 2),
             "experts_touched": rt["experts"], "pairs": rt["pairs"]}
 
 
@@ -316,6 +318,8 @@ def run_gpu(args):
         wg = [torch.empty(Tgl, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
         part = [torch.empty(Tgl, D, dtype=torch.float32, device=dev) for _ in range(n)]
         mine = [torch.empty(Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
+        recv = ([torch.empty(world, Tloc, D, dtype=torch.float32, device=dev) for _ in range(n)]
+                if args.combine == "all_to_all" else None)
         rw = [torch.empty(Tloc, K_TOP, dtype=torch.float32, device=dev) for _ in range(n)]
         ri = [torch.empty(Tloc, K_TOP, dtype=torch.int64, device=dev) for _ in range(n)]
         pev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(EP_PHASES) + 1)] for _ in range(n)]
@@ -340,10 +344,16 @@ def run_gpu(args):
                                           Tloc, L.ptr(part[i]), ws, wsn, st), "wf_moe_forward_ep")
             if ev:
                 ev[3].record()
-            dist.reduce_scatter_tensor(mine[i], part[i])
+            if recv is None:
+                dist.reduce_scatter_tensor(mine[i], part[i])
+            else:
+                dist.all_to_all_single(recv[i], part[i])
             if ev:
                 ev[4].record()
-            L.check(lib.wf_moe_to_bf16(L.ptr(mine[i]), Tloc * D, L.ptr(ys[i]), st), "wf_moe_to_bf16")
+            if recv is None:
+                L.check(lib.wf_moe_to_bf16(L.ptr(mine[i]), Tloc * D, L.ptr(ys[i]), st), "wf_moe_to_bf16")
+            else:
+                L.check(lib.wf_moe_sum_ranks(L.ptr(recv[i]), world, Tloc * D, L.ptr(ys[i]), st), "wf_moe_sum_ranks")
             if ev:
                 ev[5].record()
 
@@ -363,13 +373,13 @@ def run_gpu(args):
         for i in range(W):
             one(i)
         torch.cuda.synchronize()
-        g = None
-        if world == 1:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for i in range(W, n):
-                    one(i)
-            g.replay()  # one untimed replay (graph upload)
+        # the K timed steps as one CUDA graph (NCCL collectives included for N > 1;
+        # every rank captures the same sequence), so host launch gaps stay out
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(W, n):
+                one(i)
+        g.replay()  # one untimed replay (graph upload)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -420,7 +430,8 @@ def run_gpu(args):
         if world == 1:
             byts = [step_bytes(r, Tloc, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         else:
-            byts = [ep_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
+            byts = [ep_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts, args.combine)
+                    for r in routing]
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
         layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else ["route", "experts", "to_bf16"]))
@@ -450,7 +461,7 @@ def run_gpu(args):
     kms = main["kms"]
     # the dominant HBM-bound kernel (multi-GPU: of the compute phases; the collectives
     # are reported in kernel_us beside them)
-    dom = max((k for k in kms if k not in ("all_gather", "reduce_scatter")), key=kms.get)
+    dom = max((k for k in kms if k not in ("all_gather", "combine")), key=kms.get)
     ach = main["bytes"][dom] / (kms[dom] * 1e-3) / 1e9
     value = T * world / (main["ms"] * 1e-3)
     traffic, traffic_src = None, None
@@ -461,7 +472,7 @@ def run_gpu(args):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(layers, T, args.steps, args.warmup, dev, world, rank)
+        e2e = run_e2e(layers, T, args.steps, args.warmup, dev, world, rank, args.combine)
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 5),
@@ -475,9 +486,10 @@ def run_gpu(args):
             "routing": args.routing,
             "tokens_per_gpu": T, "global_tokens": T * world, "hidden": D, "experts": E, "inter": I,
             "topk": K_TOP, "layers_cycled": args.layers, "parallelism": f"ep{world}" if world > 1 else "single",
+            "combine": args.combine if world > 1 else None,
             "l2": f"{args.layers} distinct layers cycled (per-step weights cold in L2), no flush",
             "timing": "CUDA graph of K steps, CUDA events on the launching stream" if world == 1 else
-                      "eager steps (NCCL), CUDA events, max over ranks",
+                      "CUDA graph of K steps (NCCL collectives captured), CUDA events, max over ranks",
             "us_per_step": round(main["ms"] * 1e3, 2),
             "layer_GBps": round(main["layer_bytes"] / (main["ms"] * 1e-3) / 1e9, 1),
             "kernel_us": {k: round(v * 1e3, 2) for k, v in kms.items()},
@@ -504,7 +516,7 @@ def run_gpu(args):
         print(json.dumps(out), flush=True)
 
 
-def run_e2e(layers, T, K, W, dev, world, rank):
+def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter"):
     """Public API (MoELayer.forward), host pinned input -> device -> host output every step."""
     import torch
     import torch.distributed as dist
@@ -521,7 +533,7 @@ def run_e2e(layers, T, K, W, dev, world, rank):
             y = lay.forward(xd)
         else:
             from wanferenz_b200.ep import ep_forward
-            y = ep_forward(lay, xd)
+            y = ep_forward(lay, xd, combine=combine)
         yh[i].copy_(y, non_blocking=True)
 
     for i in range(W):
@@ -542,7 +554,8 @@ def run_e2e(layers, T, K, W, dev, world, rank):
     ms = float(ms.item()) / K
     return {"value": round(T * world / (ms * 1e-3), 1), "unit": "tokens/s",
             "us_per_step": round(ms * 1e3, 2), "h2d_bytes_per_step": T * D * 2,
-            "d2h_bytes_per_step": T * D * 2, "api": "wanferenz_b200.moe.MoELayer.forward"}
+            "d2h_bytes_per_step": T * D * 2,
+            "api": "wanferenz_b200.moe.MoELayer.forward" if world == 1 else "wanferenz_b200.ep.ep_forward"}
 
 
 # ---------------------------------------------------------------------------

@@ -168,6 +168,13 @@ int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const v
  * MoE.forward's output (architecture.py:794) after the cross-rank sum. */
 int wf_moe_to_bf16(const float *src, int64_t n, void *dst, void *stream);
 
+/* y[i] = bf16(parts[0*n + i] + parts[1*n + i] + ... + parts[(P-1)*n + i]), summed
+ * left to right in f32, for i < n (n a multiple of 4; parts 16-byte, y 8-byte
+ * aligned): the combine after an all-to-all of the ranks' partial rows, the
+ * reference's all_reduce + cast (architecture.py:791-794) in a fixed order that
+ * does not depend on the collective's algorithm. */
+int wf_moe_sum_ranks(const float *parts, int32_t P, int64_t n, void *y, void *stream);
+
 /* Expert-parallel epilogue: y[t] = bf16(y_partial_reduced[t] + shared_out[row0 + t])
  * for t < T, where shared_out is the shared expert's output that the last
  * wf_moe_forward on this workspace left in it (architecture.py:791-794, after

@@ -47,6 +47,12 @@ class OracleShard:
     def to_bf16(self, y):
         return torch.from_numpy(O.round_bf16(y.numpy().astype(np.float32))).to(torch.bfloat16)
 
+    def sum_ranks(self, parts):
+        acc = parts[0].numpy().astype(np.float32)
+        for p in range(1, parts.size(0)):
+            acc = (acc + parts[p].numpy()).astype(np.float32)
+        return torch.from_numpy(O.round_bf16(acc)).to(torch.bfloat16)
+
 
 def _free_port():
     s = socket.socket()
@@ -56,7 +62,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, T, q):
+def _worker(rank, world, port, T, q, combine="reduce_scatter"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -67,19 +73,19 @@ def _worker(rank, world, port, T, q):
         x = torch.from_numpy(O.bf16_to_f32(x16)).to(torch.bfloat16)
         mine = x[rank * T:(rank + 1) * T]
         lo, hi = shard_range(SPEC.E, world, rank)
-        y = ep_forward(OracleShard(syn, lo, hi), mine)
+        y = ep_forward(OracleShard(syn, lo, hi), mine, combine=combine)
         q.put((rank, y.float().numpy()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T", [1, 3])
-def test_ep_forward_two_ranks_matches_single_process(T):
+@pytest.mark.parametrize("T,combine", [(1, "reduce_scatter"), (3, "reduce_scatter"), (3, "all_to_all")])
+def test_ep_forward_two_ranks_matches_single_process(T, combine):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, q, combine)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=120) for _ in range(world))

@@ -255,6 +255,22 @@ def test_forward_ep_shard_without_tokens(shared_rows, engine):
         U.assert_layer_close(q[r0:r0 + n].cpu().numpy(), sh, "shared rows")
 
 
+@pytest.mark.parametrize("P", [1, 2, 8])
+def test_sum_ranks_is_ascending_rank_sum(P):
+    """wf_moe_sum_ranks: left-to-right fp32 sum over ranks, then bf16 (bit-exact)."""
+    from wanferenz_b200 import _lib as L
+
+    lib = L.load()
+    g = torch.Generator(device="cuda").manual_seed(P)
+    parts = torch.randn(P, 5, 4096, device="cuda", generator=g) * torch.logspace(-3, 3, P, device="cuda")[:, None, None]
+    acc = parts[0].clone()
+    for p in range(1, P):
+        acc = acc + parts[p]
+    out = torch.empty(5, 4096, dtype=torch.bfloat16, device="cuda")
+    L.check(lib.wf_moe_sum_ranks(L.ptr(parts), P, parts[0].numel(), L.ptr(out), L.stream_ptr()), "wf_moe_sum_ranks")
+    assert torch.equal(out, acc.to(torch.bfloat16))
+
+
 def test_to_bf16_rounds_to_nearest_even():
     from wanferenz_b200 import _lib as L
 

@@ -24,6 +24,7 @@ EXPORTS = (
     "wf_moe_finish", "wf_moe_route", "wf_moe_read_error", "wf_act_quant", "wf_fp4_act_quant",
     "wf_fp8_gemm", "wf_fp4_gemm", "wf_grouped_fp4_gemm", "wf_gemm_workspace_bytes",
     "wf_fp4_scales_in_range", "wf_moe_forward_noalloc", "wf_moe_forward_ep", "wf_moe_to_bf16",
+    "wf_moe_sum_ranks",
 )
 
 
@@ -74,6 +75,7 @@ def _declare(lib):
         "wf_moe_forward_ep": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, I32,
                                              P, P, I32, I32, P, P, SZ, P]),
         "wf_moe_to_bf16": (ctypes.c_int, [P, I64, P, P]),
+        "wf_moe_sum_ranks": (ctypes.c_int, [P, I32, I64, P, P]),
         "wf_moe_route": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, P,
                                         I32, P, P, P, SZ, P]),
         "wf_moe_read_error": (ctypes.c_int, [P, SZ, P]),

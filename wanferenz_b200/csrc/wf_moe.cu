@@ -1422,6 +1422,23 @@ __global__ void k_moe_finish(const float *yp, const __nv_bfloat16 *os, __nv_bflo
         y[i] = __float2bfloat16_rn(yp[i] + __bfloat162float(os[i]));
 }
 
+// y[i] = bf16(parts[0][i] + parts[1][i] + ... + parts[P-1][i]), left to right
+// (four consecutive elements per thread; n4 = n / 4)
+__global__ void k_sum_ranks(const float4 *parts, int P, long long n4, uint2 *y) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        float4 acc = __ldg(parts + i);
+        for (int p = 1; p < P; ++p) {
+            const float4 v = __ldg(parts + (size_t)p * n4 + i);
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        const uint32_t lo = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc.x)) |
+                            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc.y)) << 16);
+        const uint32_t hi = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc.z)) |
+                            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc.w)) << 16);
+        y[i] = make_uint2(lo, hi);
+    }
+}
+
 __global__ void k_to_bf16(const float *src, __nv_bfloat16 *dst, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         dst[i] = __float2bfloat16_rn(src[i]);
@@ -2040,6 +2057,18 @@ int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const v
     a.y = nullptr; a.y_partial = y_partial; a.partial = 1;
     a.out_w = nullptr; a.out_idx = nullptr;
     return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
+}
+
+int wf_moe_sum_ranks(const float *parts, int32_t P, int64_t n, void *y, void *stream) {
+    if (!parts || !y) return fail(WF_E_ARG, "null pointer");
+    if (P <= 0 || P > 1024) return fail(WF_E_SHAPE, "P outside 1..1024");
+    if (n <= 0 || n % 4 || n > (int64_t)1 << 30) return fail(WF_E_SHAPE, "n must be a positive multiple of 4 up to 2^30");
+    if ((uintptr_t)parts % 16 || (uintptr_t)y % 8) return fail(WF_E_ARG, "parts must be 16-byte and y 8-byte aligned");
+    const int64_t n4 = n / 4, blocks = (n4 + 255) / 256;
+    wf::k_sum_ranks<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, (cudaStream_t)stream>>>(
+        (const float4 *)parts, P, n4, (uint2 *)y);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "sum_ranks launch");
 }
 
 int wf_moe_to_bf16(const float *src, int64_t n, void *dst, void *stream) {

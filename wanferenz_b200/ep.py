@@ -10,10 +10,17 @@ batch; here each token is routed once, on the rank that owns it:
 3. one forward on the gathered batch with that routing: the rank's local
    experts on every row, the shared expert on the rank's own rows only
    (``MoELayer.forward_ep``) -> fp32 partial sums ``[P*T, D]``;
-4. reduce-scatter: each rank receives the sum over ranks for its own rows
-   (the reference's ``dist.all_reduce(y)``, architecture.py:791-792,
-   restricted to those rows), shared expert included (793);
-5. cast to bf16 (794).
+4. combine: each rank receives the sum over ranks for its own rows (the
+   reference's ``dist.all_reduce(y)``, architecture.py:791-792, restricted to
+   those rows), shared expert included (793), cast to bf16 (794); either
+   ``reduce_scatter`` (NCCL reduces, in its own order) or ``all_to_all`` (each
+   rank receives the other ranks' partial rows and sums them in ascending rank
+   order: the same bytes, one more kernel, results independent of the
+   collective's algorithm).
+
+The dispatch is an all-gather: every rank needs every token's row (its
+experts may be among the token's k), so a fixed-capacity all-to-all would move
+the same bytes.
 """
 
 from __future__ import annotations
@@ -38,8 +45,13 @@ def gather_tokens(x, w, idx, xg, wg, ig, group=None):
         dist.all_gather_into_tensor(ig, idx, group=group)
 
 
-def ep_forward(layer, x, input_ids=None, group=None):
+COMBINES = ("reduce_scatter", "all_to_all")
+
+
+def ep_forward(layer, x, input_ids=None, group=None, combine="reduce_scatter"):
     """One expert-parallel MoE forward of this rank's ``x [T, D]`` (T equal on all ranks)."""
+    if combine not in COMBINES:
+        raise ValueError(f"combine must be one of {COMBINES}")
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     T = x.size(0)
@@ -50,6 +62,10 @@ def ep_forward(layer, x, input_ids=None, group=None):
     ig = torch.empty(world * T, idx.size(1), dtype=idx.dtype, device=x.device)
     gather_tokens(x, w.contiguous(), idx.contiguous(), xg, wg, ig, group)
     part = layer.forward_ep(xg, wg, ig, shared_rows=(rank * T, T))
+    if combine == "all_to_all":
+        recv = torch.empty(world, T, x.size(1), dtype=torch.float32, device=x.device)
+        dist.all_to_all_single(recv, part, group=group)
+        return layer.sum_ranks(recv)
     mine = torch.empty(T, x.size(1), dtype=torch.float32, device=x.device)
     dist.reduce_scatter_tensor(mine, part, group=group)
     return layer.to_bf16(mine)

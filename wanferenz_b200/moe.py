@@ -211,6 +211,16 @@ class MoELayer:
         L.check(self.lib.wf_moe_to_bf16(L.ptr(y), y.numel(), L.ptr(o), L.stream_ptr()), "wf_moe_to_bf16")
         return o
 
+    def sum_ranks(self, parts, out=None):
+        """``bf16(parts[0] + ... + parts[P-1])`` of fp32 ``parts [P, T, D]``, summed in
+        ascending rank order (``wf_moe_sum_ranks``)."""
+        parts = parts.contiguous()
+        P = parts.size(0)
+        o = out if out is not None else torch.empty(parts.shape[1:], dtype=torch.bfloat16, device=parts.device)
+        L.check(self.lib.wf_moe_sum_ranks(L.ptr(parts), P, parts[0].numel(), L.ptr(o), L.stream_ptr()),
+                "wf_moe_sum_ranks")
+        return o
+
     def route(self, x, input_ids=None):
         """``Gate.forward`` (architecture.py:696-718): ``(weights [T,k] f32, indices [T,k] int64)``."""
         x = x.contiguous()
