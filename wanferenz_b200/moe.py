@@ -146,6 +146,8 @@ class MoELayer:
             if input_ids is None:
                 raise WfUnsupported("hash layers need input_ids")
             input_ids = input_ids.reshape(-1).to(torch.int64).contiguous()
+        if partial and T > self.max_tokens:
+            raise WfUnsupported("partial mode needs T <= max_tokens (the shared output is per call)")
         if partial:
             y = out if out is not None else torch.empty(T, self.dim, dtype=torch.float32, device=x.device)
         else:
@@ -167,8 +169,6 @@ class MoELayer:
                 L.ptr(rw[t0:t1]) if routing else 0, L.ptr(ri[t0:t1]) if routing else 0,
                 L.ptr(self.workspace), self.workspace.numel(), st)
             L.check(rc, "wf_moe_forward")
-            if partial and t1 < T:
-                raise WfUnsupported("partial mode needs T <= max_tokens (the shared output is per call)")
         return (y, rw, ri) if routing else y
 
     __call__ = forward
@@ -317,11 +317,43 @@ def bank_layout(module, preserve=True, max_tokens=64):
     return n
 
 
+def _decline(self, x, input_ids, why):
+    """The reference plugins' convention for a configuration they do not cover
+    (fp4_grouped.py:256-262): count the reason and run the replaced forward."""
+    counts = getattr(self, "_wf_declined", None)
+    if counts is None:
+        counts = self._wf_declined = {}
+    counts[why] = counts.get(why, 0) + 1
+    return _REF_FORWARD(self, x, input_ids)
+
+
 def b200_forward(self, x, input_ids):
-    """Replacement of ``MoE.forward`` (architecture.py:777-794) on the B200 kernels."""
+    """Replacement of ``MoE.forward`` (architecture.py:777-794) on the B200 kernels.
+
+    A configuration the kernels do not cover (``WfUnsupported``: experts not
+    FP4, shared expert not FP8, shapes outside the kernels' limits, a batch over
+    the workspace in the all-reduce mode) declines to the replaced forward and
+    is counted in ``self._wf_declined``; a missing CUDA device or library and
+    CUDA errors raise.  Successful steps count in ``self._wf_steps``.
+    """
     layer = getattr(self, "_wf_layer", None)
+    if layer is False:
+        return _decline(self, x, input_ids, self._wf_unsupported)
     if layer is None:
-        self._wf_layer = layer = _layer_from_module(self, _MOD)
+        try:
+            self._wf_layer = layer = _layer_from_module(self, _MOD)
+        except WfUnsupported as e:
+            self._wf_layer, self._wf_unsupported = False, str(e)
+            return _decline(self, x, input_ids, str(e))
+    try:
+        y = _b200_step(self, layer, x, input_ids)
+    except WfUnsupported as e:
+        return _decline(self, x, input_ids, str(e))
+    self._wf_steps = getattr(self, "_wf_steps", 0) + 1
+    return y
+
+
+def _b200_step(self, layer, x, input_ids):
     shape = x.size()
     xv = x.view(-1, self.dim)
     ids = input_ids.flatten() if input_ids is not None else None
@@ -334,7 +366,6 @@ def b200_forward(self, x, input_ids):
         y = layer.finish(yp)
     else:
         y = layer.forward(xv, ids)
-    self._wf_steps = getattr(self, "_wf_steps", 0) + 1
     return y.view(shape)
 
 
