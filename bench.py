@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--routing", default="uniform", choices=("uniform", "zipf"),
                     help="zipf: BASELINE config 4 popularity, gate bias += beta*log(rank^-1.2)")
     ap.add_argument("--zipf-beta", type=float, default=0.06)
+    ap.add_argument("--suite", default="moe", choices=("moe", "fp8_gemm"),
+                    help="fp8_gemm: BASELINE config 3, the FP8 block-scaled GEMM sweep (one JSON line, N=1)")
     ap.add_argument("--combine", default="reduce_scatter", choices=("reduce_scatter", "all_to_all"),
                     help="N > 1: NCCL reduce-scatter of the partials, or all-to-all + ascending-rank sum")
     ap.add_argument("--init", default="quant", choices=("quant", "random"),
@@ -647,10 +649,78 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_fp8_gemm_suite(args):
+    """``fp8_gemm`` (architecture.py:121-134 -> torch_ops.py:93-99) for
+    M in {1, 2, 4, 8, 16} and the four (N, K) of the model's dense projections, E4M3
+    weights with one fp32 (config 3) or e8m0 (model path) scale per 128x128 block,
+    bf16 activations quantized per token (1x128 fp32 scales).  Each point: R calls
+    cycling enough weight copies to exceed L2, captured in a CUDA graph, replayed and
+    timed with CUDA events.  Bytes per call: N*K + scales + M*K*2 + M*N*2."""
+    import torch
+
+    from wanferenz_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, peak_kind = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    res = []
+    for (N, K) in ((4096, 4096), (12288, 4096), (4096, 16384), (129280, 4096)):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        q, s8 = fp8_block_quant_torch(w)
+        del w
+        s32 = s8.view(torch.float8_e8m0fnu).float()
+        wq = q.view(torch.float8_e4m3fn)
+        copies = max(1, -(-300_000_000 // (N * K)))
+        wqs = [wq] + [wq.clone() for _ in range(copies - 1)]
+        # f32: config 3 as stated (fp32 scales on both sides); e8m0: the model path
+        # (scale_fmt="ue8m0", e8m0 scales on both sides, architecture.py:121-134)
+        for kind, bs in (("f32", s32), ("e8m0", s8.view(torch.float8_e8m0fnu))):
+            for M in (1, 2, 4, 8, 16):
+                x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+                if kind == "f32":
+                    aq, a_s = ops.act_quant(x, 128)
+                else:
+                    aq, a_s = ops.act_quant(x, 128, scale_fmt="ue8m0", scale_dtype=torch.float8_e8m0fnu)
+                R = 4 * copies if copies > 1 else 8
+                for _ in range(3):  # warm-up (workspace growth, module load)
+                    ops.fp8_gemm(aq, a_s, wqs[0], bs)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for r in range(R):
+                        ops.fp8_gemm(aq, a_s, wqs[r % copies], bs)
+                graph.replay()
+                torch.cuda.synchronize()
+                t0 = torch.cuda.Event(enable_timing=True)
+                t1 = torch.cuda.Event(enable_timing=True)
+                reps = 5
+                t0.record()
+                for _ in range(reps):
+                    graph.replay()
+                t1.record()
+                torch.cuda.synchronize()
+                us = t0.elapsed_time(t1) * 1e3 / (reps * R)
+                del graph
+                nbytes = N * K + (N // 128) * (K // 128) * (4 if kind == "f32" else 1) + M * K * 2 + M * N * 2
+                gbs = nbytes / (us * 1e-6) / 1e9
+                res.append({"N": N, "K": K, "M": M, "scale": kind, "us": round(us, 2),
+                            "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
+        del wqs, wq, q, s8, s32
+        torch.cuda.empty_cache()
+    out = {"suite": "fp8_gemm", "metric": "FP8 block-scaled GEMM us/call (BASELINE config 3)",
+           "unit": "us", "higher_is_better": False, "peak_GBps": hbm, "peak_kind": peak_kind,
+           "timing": "CUDA graph of R calls over weight copies > L2, CUDA events", "results": res}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.suite == "fp8_gemm":
+        run_fp8_gemm_suite(args)
     else:
         run_gpu(args)
 

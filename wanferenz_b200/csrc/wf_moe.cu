@@ -2226,12 +2226,26 @@ static int gemm_chunks(int64_t K) { return (int)((K + wf::KMAX - 1) / wf::KMAX);
 
 // K chunks of the tcgen05 dense path: at least enough to fill ~2 items per SM
 // when there are few 128-row tiles, each chunk a multiple of 128 and <= 4096.
-static int tc_chunks(int64_t M, int64_t N, int64_t K) {
-    int nkc = gemm_chunks(K);
+// K split of the tcgen05 dense GEMM: the number of chunks that minimizes an
+// estimate of the kernel time.  Items (16 tokens x 128 rows x one K chunk) are
+// dealt to the SMs in rounds; an item costs its K steps at the per-SM share of
+// the streaming rate (5.5 TB/s over 148 SMs, ~37 GB/s; 16 KB of HBM per step
+// for E4M3, 8 KB for E2M1) plus ~2 us of fixed work (B operand, scales,
+// epilogue), and the split-K sum adds ~0.5 us per chunk.  A finer split only
+// pays while it fills idle SMs.
+static int tc_chunks(int64_t M, int64_t N, int64_t K, bool fp4) {
+    const int64_t sms = std::max(1, sm_count());
     const int64_t items = ((M + 15) / 16) * (N / 128);
-    const int want = 2 * std::max(1, sm_count());
-    while (items * nkc < want && K % (128 * (nkc * 2)) == 0 && nkc < 16) nkc *= 2;
-    return nkc;
+    const double step_us = (fp4 ? 8192.0 : 16384.0) / 37.0e3;
+    int best = 0;
+    double best_us = 1e30;
+    for (int nkc = gemm_chunks(K); nkc <= 16; nkc *= 2) {
+        if (K % (128 * nkc) || K / nkc > wf::tc::KC_MAX) continue;
+        const int64_t rounds = (items * nkc + sms - 1) / sms;
+        const double us = (double)rounds * ((double)(K / nkc / 128) * step_us + 2.0) + (nkc > 1 ? 0.5 * nkc : 0.0);
+        if (us < best_us) { best_us = us; best = nkc; }
+    }
+    return best > 0 ? best : gemm_chunks(K);
 }
 
 static int gemm_rows(int wfmt, int64_t N, int64_t K) {
@@ -2272,7 +2286,9 @@ size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     // sized for the finer of the FP8 / FP4 row blockings, and for the tcgen05 split-K
     const int rows = std::min(gemm_rows(wf::FMT_FP8, N, K), gemm_rows(wf::FMT_FP4, N, K));
     size_t need = gemm_ws(M, N, K, rows).total;
-    if (N % 128 == 0 && K % 128 == 0) need = std::max(need, gemm_ws_tc(M, N, K, tc_chunks(M, N, K)).total);
+    if (N % 128 == 0 && K % 128 == 0)
+        need = std::max({need, gemm_ws_tc(M, N, K, tc_chunks(M, N, K, false)).total,
+                         gemm_ws_tc(M, N, K, tc_chunks(M, N, K, true)).total});
     return need;
 }
 
@@ -2296,7 +2312,7 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     const bool tc_ok = !tc_disabled() && G == 0 && a_kind == WF_SCALE_E8M0 && b_kind == WF_SCALE_E8M0 &&
                        N % 128 == 0 && (K / nkc) <= wf::tc::KC_MAX && ((uintptr_t)b % 32) == 0;
     if (tc_ok) {
-        const int tnkc = tc_chunks(M, N, K);
+        const int tnkc = tc_chunks(M, N, K, wfmt == wf::FMT_FP4);
         const GemmWs Lt = gemm_ws_tc(M, N, K, tnkc);
         if (ws_bytes < Lt.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
         if (tnkc > 1) {  // the workspace serves every shape: its counters start at zero per call

@@ -358,12 +358,22 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
-                    for (int m = 0; m < ie.ntok; ++m) {
-                        float acc = 0.f;
-                        for (int c = 0; c < d.nkc; ++c)
-                            acc += __ldcg(d.part + ((size_t)c * d.M + ie.tok0 + m) * d.N + row);
-                        d.out[(size_t)(ie.tok0 + m) * d.N + row] = __float2bfloat16_rn(acc);
+                    // chunk outer, tokens inner: the tokens' loads of one chunk are in
+                    // flight together; each token's sum still runs in chunk order
+                    float acc[NTOK];
+#pragma unroll
+                    for (int m = 0; m < NTOK; ++m) acc[m] = 0.f;
+                    for (int c = 0; c < d.nkc; ++c) {
+                        const float *pc = d.part + ((size_t)c * d.M + ie.tok0) * d.N + row;
+                        float v[NTOK];
+#pragma unroll
+                        for (int m = 0; m < NTOK; ++m) v[m] = m < ie.ntok ? __ldcg(pc + (size_t)m * d.N) : 0.f;
+#pragma unroll
+                        for (int m = 0; m < NTOK; ++m) acc[m] += v[m];
                     }
+#pragma unroll
+                    for (int m = 0; m < NTOK; ++m)
+                        if (m < ie.ntok) d.out[(size_t)(ie.tok0 + m) * d.N + row] = __float2bfloat16_rn(acc[m]);
                     if (lane == 0) *cnt = 0u;
                 }
             }
