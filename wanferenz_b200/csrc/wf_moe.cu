@@ -2292,6 +2292,28 @@ size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     return need;
 }
 
+// The split-K counters of a GEMM workspace return to zero at the end of every
+// call (the last chunk of each tile resets its counter), but where the counter
+// and partial regions lie depends on the shape, so a workspace is cleared when
+// the shape it serves changes.  Skipping the clear otherwise keeps consecutive
+// GEMMs of one shape adjacent on the stream, so programmatic dependent launch
+// overlaps each one's set-up and weight stream with the previous one.
+struct GemmShape {
+    int64_t M, N, K;
+    int fmt;
+    bool operator==(const GemmShape &o) const { return M == o.M && N == o.N && K == o.K && fmt == o.fmt; }
+};
+static std::mutex g_gemm_shape_mu;
+static std::map<const void *, GemmShape> g_gemm_shape;
+
+static bool gemm_shape_changed(const void *ws, const GemmShape &sh) {
+    std::lock_guard<std::mutex> lock(g_gemm_shape_mu);
+    auto it = g_gemm_shape.find(ws);
+    if (it != g_gemm_shape.end() && it->second == sh) return false;
+    g_gemm_shape[ws] = sh;
+    return true;
+}
+
 static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const void *b,
                  const void *b_s, int b_kind, int64_t M, int64_t N, int64_t K, int64_t G,
                  void *out, void *ws, size_t ws_bytes, cudaStream_t st) {
@@ -2315,7 +2337,7 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
         const int tnkc = tc_chunks(M, N, K, wfmt == wf::FMT_FP4);
         const GemmWs Lt = gemm_ws_tc(M, N, K, tnkc);
         if (ws_bytes < Lt.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
-        if (tnkc > 1) {  // the workspace serves every shape: its counters start at zero per call
+        if (tnkc > 1 && gemm_shape_changed(ws, GemmShape{M, N, K, wfmt})) {
             cudaError_t e0 = cudaMemsetAsync((uint8_t *)ws + Lt.cnt, 0, Lt.part - Lt.cnt, st);
             if (e0 != cudaSuccess) return cuda_fail(e0, "cudaMemsetAsync(gemm counters)");
         }
@@ -2331,8 +2353,18 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
         t.part = (float *)((uint8_t *)ws + Lt.part);
         const int G_ = sm_count();
         if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
-        wf::tc::k_dense_tc<<<G_, wf::tc::THREADS, wf::tc::SMEM, st>>>(t);
-        cudaError_t e = cudaGetLastError();
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(G_);
+        lc.blockDim = dim3(wf::tc::THREADS);
+        lc.dynamicSmemBytes = wf::tc::SMEM;
+        lc.stream = st;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&lc, wf::tc::k_dense_tc, t);
+        if (e == cudaSuccess) e = cudaGetLastError();
         return e == cudaSuccess ? WF_OK : cuda_fail(e, "tc gemm launch");
     }
     wf::DenseArgs d;
@@ -2345,6 +2377,8 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     d.rows = rows;
     d.cnt = (unsigned *)((uint8_t *)ws + L.cnt);
     d.part = (float *)((uint8_t *)ws + L.part);
+    // this engine lays the workspace out differently: the next tcgen05 call clears it
+    gemm_shape_changed(ws, GemmShape{M, N, K, -1 - wfmt});
     if (nkc > 1) {  // the workspace serves every shape: its counters start at zero per call
         cudaError_t e0 = cudaMemsetAsync((uint8_t *)ws + L.cnt, 0, L.part - L.cnt, st);
         if (e0 != cudaSuccess) return cuda_fail(e0, "cudaMemsetAsync(gemm counters)");

@@ -249,6 +249,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Bars B = bars_at(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Programmatic dependent launch: set-up and the weight stream (constant
+    // data) overlap the previous kernel; the worker warps, which read the
+    // activations and write every output, wait for it first.
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, 1); }
         mbar_init(B.b_ready, 4);
@@ -322,6 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
         }
     } else {
         // ---- worker warps: B operand, scale factors, epilogue ----
+        pdl_wait();
         const int wq = warp & 3;          // TMEM lane quadrant of this warp
         const int wt = threadIdx.x - W_WORK0 * 32;  // 0..127
         const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
@@ -363,6 +368,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
                     float acc[NTOK];
 #pragma unroll
                     for (int m = 0; m < NTOK; ++m) acc[m] = 0.f;
+#pragma unroll 4
                     for (int c = 0; c < d.nkc; ++c) {
                         const float *pc = d.part + ((size_t)c * d.M + ie.tok0) * d.N + row;
                         float v[NTOK];
