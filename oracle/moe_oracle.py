@@ -303,7 +303,9 @@ def topk_margin(biased: np.ndarray, topk: int) -> np.ndarray:
 
 
 def _silu(g):
-    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    # exp(-g) overflows to inf for g < -88: g / inf = -0, silu's limit
+    with np.errstate(over="ignore"):
+        return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
 
 
 def expert_fp4(x, w1, w1_s, w3, w3_s, w2, w2_s, weights=None, swiglu_limit=0.0, ue8m0=True, acc=np.float64):

@@ -34,8 +34,9 @@ def gather_tokens(x, w, idx, xg, wg, ig, group=None):
     """All-gathers tokens ``x [T, D]`` and their routing ``w [T, k]``, ``idx [T, k]``
     into ``xg, wg, ig [P*T, ...]`` (rank r's rows at ``r*T``).  On NCCL the three
     gathers are issued as one group, so they cost one collective launch."""
-    if dist.get_backend(group) == "nccl":
-        with c10d._coalescing_manager(group, x.device):
+    coalesce = getattr(c10d, "_coalescing_manager", None)  # a private torch API: used when present
+    if coalesce is not None and dist.get_backend(group) == "nccl":
+        with coalesce(group, x.device):
             dist.all_gather_into_tensor(xg, x, group=group)
             dist.all_gather_into_tensor(wg, w, group=group)
             dist.all_gather_into_tensor(ig, idx, group=group)
