@@ -68,3 +68,22 @@ def test_shape_errors_before_any_launch():
     assert lib.wf_fp4_act_quant(p, 2, 48, p, p, None) == L.WF_E_SHAPE
     assert lib.wf_fp8_gemm(p, p, 0, p, p, 0, 1, 16, 100, p, p, 256, None) == L.WF_E_SHAPE
     assert lib.wf_fp8_gemm(p, p, 5, p, p, 0, 1, 16, 128, p, p, 256, None) == L.WF_E_DTYPE
+
+
+def test_expert_parallel_entry_points_validate_before_launch():
+    lib = L.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: every check below precedes any launch
+    w = L.MoeWeights()
+    for f in ("w13", "w13_s", "w2", "w2_s", "shared_w13", "shared_s13", "shared_w2", "shared_s2", "gate_w"):
+        setattr(w, f, 16)
+    cfg = ctypes.byref(_cfg())
+    # routing and output are required
+    assert lib.wf_moe_forward_ep(cfg, ctypes.byref(w), p, 4, None, p, 0, 4, p, p, 1 << 40, None) == L.WF_E_ARG
+    # the shared-expert window must lie inside the batch
+    for r0, n in ((-1, 1), (0, 5), (3, 2), (0, -1)):
+        assert lib.wf_moe_forward_ep(cfg, ctypes.byref(w), p, 4, p, p, r0, n, p, p, 1 << 40, None) == L.WF_E_SHAPE
+    assert lib.wf_moe_to_bf16(None, 8, p, None) == L.WF_E_ARG
+    assert lib.wf_moe_to_bf16(p, 0, p, None) == L.WF_E_SHAPE
+    assert lib.wf_moe_sum_ranks(p, 0, 8, p, None) == L.WF_E_SHAPE       # no ranks
+    assert lib.wf_moe_sum_ranks(p, 2, 6, p, None) == L.WF_E_SHAPE       # n not a multiple of 4
+    assert lib.wf_moe_sum_ranks(ctypes.c_void_p(24), 2, 8, p, None) == L.WF_E_ARG  # parts misaligned

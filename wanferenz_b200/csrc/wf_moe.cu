@@ -2054,12 +2054,12 @@ int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const v
     int rc = check_expert_ptrs(w);
     if (rc) return rc;
     if (!in_weights || !in_indices || !y_partial) return fail(WF_E_ARG, "null routing or output");
+    if (shared_row0 < 0 || shared_rows < 0 || (int64_t)shared_row0 + shared_rows > T)
+        return fail(WF_E_SHAPE, "shared rows outside 0..T");
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
     rc = fill_args(cfg, w, x, nullptr, T, workspace, workspace_bytes, a, &t, true);
     if (rc) return rc;
-    if (shared_row0 < 0 || shared_rows < 0 || shared_row0 + shared_rows > T)
-        return fail(WF_E_SHAPE, "shared rows outside 0..T");
     a.given = 1;
     a.in_w = in_weights; a.in_idx = (const long long *)in_indices;
     a.sh0 = shared_row0; a.shT = shared_rows; a.sh_add = 1;
