@@ -226,7 +226,12 @@ int wf_grouped_fp4_gemm(const void *a, const void *a_s, int32_t a_scale_kind, co
                         const void *w_s, int64_t G, int64_t N, int64_t K, void *out,
                         void *workspace, size_t workspace_bytes, void *stream);
 
-/* Workspace bytes for the dense GEMM entry points above. */
+/* Workspace bytes for the dense GEMM entry points above.  The workspace is
+ * zero-filled once when allocated; its split-K counters return to zero at
+ * the end of every call.  The library clears them again only when the shape
+ * (or the engine) a workspace serves changes, so a workspace is used by one
+ * stream at a time, and a call that failed (WF_E_TIMEOUT in the error word,
+ * the first 4 bytes) leaves it to be re-zeroed by the caller. */
 size_t wf_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 /* Load-time check that no FP4 weight scale byte is 0 or 255 (2^-127, the
