@@ -1240,15 +1240,6 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
     init_smem(sm);
-    if (a.tc && !a.route_only && a.shT > 0 && (threadIdx.x >> 5) == NCW) {
-        // The shared expert's weights do not depend on the routing: this CTA's
-        // slice of them goes to L2 now, while HBM is idle during the router, the
-        // top-k and the tables (a hint: nothing waits for it).
-        const size_t b13 = (size_t)2 * a.I * a.D, b2 = (size_t)a.D * a.I;
-        const size_t G = gridDim.x, c = blockIdx.x;
-        prefetch_l2_span(a.sw13, b13 * c / G, b13 * (c + 1) / G, threadIdx.x & 31, 32);
-        prefetch_l2_span(a.sw2, b2 * c / G, b2 * (c + 1) / G, threadIdx.x & 31, 32);
-    }
     pdl_wait();
     pdl_launch_dependents();
     const bool given = a.given;

@@ -67,25 +67,6 @@ __device__ __forceinline__ bool wf_wait(uint64_t *bar, uint32_t parity, int *err
     return true;
 }
 
-// ---- L2 prefetch hints (bulk, no completion) -------------------------------
-// Brings [src, src + bytes) into L2; src 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
-// The part [lo, hi) of the 16-byte aligned buffer p[0, bytes) in 64 KB pieces,
-// piece j issued by thread j mod nth of the caller's group (tid in 0..nth-1).
-__device__ __forceinline__ void prefetch_l2_span(const void *p, size_t lo, size_t hi, int tid, int nth) {
-    constexpr size_t PIECE = 65536;
-    lo &= ~(size_t)15;
-    hi &= ~(size_t)15;
-    const uint8_t *b = static_cast<const uint8_t *>(p);
-    for (size_t off = lo + (size_t)tid * PIECE; off < hi; off += (size_t)nth * PIECE) {
-        const size_t n = hi - off < PIECE ? hi - off : PIECE;
-        prefetch_l2_bulk(b + off, (uint32_t)n);
-    }
-}
-
 // ---- bulk copy (TMA, non-tensor) global -> shared, completes on mbarrier --
 // dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
