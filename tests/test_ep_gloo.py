@@ -1,4 +1,4 @@
-"""Expert-parallel host logic on 2 CPU ranks (gloo).
+"""Expert-parallel host logic on 2 and 4 CPU ranks (gloo).
 
 ``wanferenz_b200.ep.ep_forward`` (route the owned tokens, all-gather tokens
 and routing, local experts on the gathered batch with the given routing plus
@@ -79,23 +79,24 @@ def _worker(rank, world, port, T, q, combine="reduce_scatter"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T,combine", [(1, "reduce_scatter"), (3, "reduce_scatter"), (3, "all_to_all")])
-def test_ep_forward_two_ranks_matches_single_process(T, combine):
-    world = 2
+@pytest.mark.parametrize("world,T,combine", [(2, 1, "reduce_scatter"), (2, 3, "reduce_scatter"),
+                                             (2, 3, "all_to_all"), (4, 2, "reduce_scatter"),
+                                             (4, 2, "all_to_all")])
+def test_ep_forward_matches_single_process(world, T, combine):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, T, q, combine)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=120) for _ in range(world))
+    out = dict(q.get(timeout=180) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     syn = F.SyntheticLayer(SPEC)
     x16, _ = syn.activations(T * world, draw=5)
     y_ref, _, _ = O.moe_forward(O.bf16_to_f32(x16), syn.params(), None)
-    got = np.concatenate([out[0], out[1]])
+    got = np.concatenate([out[r] for r in range(world)])
     d = np.abs(got - y_ref)
     assert d.mean() <= 2e-3
     assert (d / np.maximum(np.abs(y_ref), 0.01 * np.sqrt((y_ref ** 2).mean()))).max() <= 1e-2
