@@ -18,8 +18,9 @@ and a reduce-scatter returns each rank its tokens' sums (the reference's
 all-reduce, architecture.py:791-792, restricted to the owner's rows).
 
 ``--impl reference`` times the reference algorithm on the host cores: the
-numpy oracle port (the reference itself is Python/TileLang and is not
-installed on the GPU box).
+torch CPU restatement of the reference's path (``oracle/torch_port.py``,
+bit-identical to the reference on its golden cases; the reference itself is
+Python/TileLang and is not installed on the GPU box).
 
 Prints ONE JSON line (rank 0).
 """
@@ -593,29 +594,40 @@ def cpu_layer(seed=0):
     return syn, params
 
 
-def cpu_forward_time(T, reps=1, seed=0):
-    import numpy as np
+def cpu_forward_time(T, reps=1, seed=0, warmup=0):
+    """Seconds per config-2 layer forward of T tokens by the torch CPU restatement of the
+    reference's path (``oracle/torch_port.py``: the reference's ops, all host threads)."""
+    import torch
 
     from oracle import moe_oracle as O
+    from oracle import torch_port as P
 
+    torch.set_num_threads(os.cpu_count())
     syn, params = cpu_layer(seed)
     times = []
-    for rep in range(reps):
+    for rep in range(warmup + reps):
         x16, _ = syn.activations(T, draw=100 + rep)
         x = O.bf16_to_f32(x16)
+        # the synthetic expert bytes are made on first use: outside the timed region
+        _, idx = P.gate(P._t(x), params)
+        for e in idx.unique().tolist():
+            params["experts"](e)
         t = time.perf_counter()
-        O.moe_forward(x, params, acc=np.float32)
-        times.append(time.perf_counter() - t)
+        P.moe_forward(x, params)
+        if rep >= warmup:
+            times.append(time.perf_counter() - t)
     return times
 
 
 def cpu_baseline(T):
-    t = cpu_forward_time(T, reps=1)
-    s = float(np.median(t)) if (np := __import__("numpy")) else t[0]
+    import numpy as np
+
+    t = cpu_forward_time(T, reps=2, warmup=1)
+    s = float(np.median(t))
     return {"value": round(T / s, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one config-2 layer forward of {T} tokens by the numpy oracle port of the "
-                      f"reference's torch CPU path (fp32 BLAS, {os.cpu_count()} host threads); "
-                      f"{s:.2f} s"}
+            "sample": f"config-2 layer forwards of {T} tokens (median of 2 after 1 warm-up) by the torch "
+                      f"CPU restatement of the reference's path (oracle/torch_port.py: the reference's "
+                      f"ops, fp32 BLAS, {os.cpu_count()} host threads); {s:.2f} s each"}
 
 
 def run_reference(args):
@@ -625,12 +637,10 @@ def run_reference(args):
     if rank != 0:
         return
     T = args.tokens
-    sample = min(T, 2)
-    for _ in range(args.warmup):
-        cpu_forward_time(sample, reps=1, seed=1)
-    times = []
-    for i in range(args.steps):
-        times.extend(cpu_forward_time(sample, reps=1, seed=2 + (i % 4)))
+    # each step a bounded sample of the workload: 4 of its tokens (~2.3 s on 8 cores)
+    sample = min(T, 4)
+    cpu_forward_time(sample, reps=0, warmup=max(args.warmup, 1), seed=1)
+    times = cpu_forward_time(sample, reps=args.steps, seed=2)
     s = sum(times) / len(times)
     value = sample / s
     out = {
@@ -642,8 +652,9 @@ def run_reference(args):
                    "tokens_per_gpu": T, "sample_tokens_per_step": sample},
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": os.cpu_count(),
                          "kind": "port",
-                         "sample": f"{sample} of the {T} tokens per step through the numpy oracle port of "
-                                   f"the reference's torch CPU MoE.forward (fp32 BLAS, all host threads)"},
+                         "sample": f"{sample} of the {T} tokens per step through the torch CPU restatement "
+                                   f"of the reference's MoE.forward (oracle/torch_port.py; the reference's "
+                                   f"ops, fp32 BLAS, all host threads)"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
