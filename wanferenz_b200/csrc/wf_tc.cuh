@@ -249,9 +249,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Bars B = bars_at(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // Programmatic dependent launch: set-up and the weight stream (constant
-    // data) overlap the previous kernel; the worker warps, which read the
-    // activations and write every output, wait for it first.
+    // Programmatic dependent launch: set-up and the first ring of weight loads
+    // (constant data) overlap the previous kernel; every thread waits for it
+    // before its first bounded wait, and the worker warps, which read the
+    // activations and write every output, before anything else.
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(B.full + s, 1); mbar_init(B.empty + s, 1); }
@@ -283,6 +284,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
                 const DItem it = dense_item(d, i);
                 for (int s = 0; s < nks; ++s, ++gs) {
                     const int st = gs % STAGES;
+                    // the first ring of weight loads overlaps the previous kernel; no
+                    // bounded wait starts before that kernel is complete
+                    if (gs == STAGES) pdl_wait();
                     if (gs >= STAGES && !twait(B.empty + st, ((gs / STAGES) - 1) & 1, d.err, B.abort)) break;
                     mbar_arrive_expect_tx(B.full + st, d.fp4 ? ABOX / 2 : ABOX);
                     tma_load_2d(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, B.full + st);
@@ -291,6 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
         }
     } else if (warp == W_MMA) {
         if (lane == 0) {
+            pdl_wait();
             int gs = 0, nb = 0, key = -1;
             const int afmt = d.fp4 ? 5 : 0;
             for (int q = 0, i = i0; i < i1 && !*B.abort; ++i, ++q) {
