@@ -17,10 +17,16 @@ local experts on the gathered batch (plus the shared expert on its own rows),
 and a reduce-scatter returns each rank its tokens' sums (the reference's
 all-reduce, architecture.py:791-792, restricted to the owner's rows).
 
-``--impl reference`` times the reference algorithm on the host cores: the
-torch CPU restatement of the reference's path (``oracle/torch_port.py``,
-bit-identical to the reference on its golden cases; the reference itself is
-Python/TileLang and is not installed on the GPU box).
+``--impl reference`` times the reference algorithm on the host cores, every
+step a forward of all ``--tokens`` tokens: the torch CPU restatement of the
+reference's path (``oracle/torch_port.py``, bit-identical to the reference on
+its golden cases; the reference itself is Python/TileLang and is not
+installed on the GPU box).  Both arms print the same ``config`` (the workload
+identity); measurements go to ``detail`` and ``timing``.
+
+The default line also carries, in ``detail``, the T = 1 / 4 / 16 sweep,
+BASELINE config 4 (64 tokens, Zipf(1.2) routing) and config 3 (the FP8
+block-scaled GEMM at M = 1 and 16); ``--no-extras`` skips the last two.
 
 Prints ONE JSON line (rank 0).
 """
@@ -58,7 +64,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--routing", default="uniform", choices=("uniform", "zipf"),
                     help="zipf: BASELINE config 4 popularity, gate bias += beta*log(rank^-1.2)")
-    ap.add_argument("--zipf-beta", type=float, default=0.06)
+    ap.add_argument("--zipf-beta", type=float, default=0.08)
+    ap.add_argument("--replays", type=int, default=10,
+                    help="timed replays of the K-step graph; the median replay gives the step time")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-3 and config-4 sub-results of the default line")
     ap.add_argument("--suite", default="moe", choices=("moe", "fp8_gemm"),
                     help="fp8_gemm: BASELINE config 3, the FP8 block-scaled GEMM sweep (one JSON line, N=1)")
     ap.add_argument("--combine", default="reduce_scatter", choices=("reduce_scatter", "all_to_all"),
@@ -75,6 +85,30 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def workload_config(args, world):
+    """The workload identity, the same in both arms' JSON lines (measurements go elsewhere)."""
+    T = args.tokens
+    if args.routing == "uniform":
+        wl = f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing"
+    else:
+        wl = (f"BASELINE config 4: config-2 layer, {T} tokens per GPU, Zipf(1.2) routing "
+              f"(gate bias += {args.zipf_beta} * log(rank^-1.2))")
+    return {"workload": wl, "routing": args.routing, "tokens_per_gpu": T, "global_tokens": T * world,
+            "hidden": D, "experts": E, "inter": I, "topk": K_TOP,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": f"{args.layers} distinct layers cycled (per-step weights cold in L2), no flush"}
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ---------------------------------------------------------------------------
@@ -306,8 +340,9 @@ def run_gpu(args):
         if world > 1:
             dist.barrier()
 
-    def measure(Tloc, K, W):
-        """K graph-captured steps (headline time) + K eager steps with per-kernel events."""
+    def measure(lays, Tloc, K, W, R):
+        """K graph-captured steps replayed R times (headline: the median replay) + K eager
+        steps with per-kernel events."""
         n = K + W
         Tgl = Tloc * world
         xs = [torch.randn(Tloc, D, device=dev).to(torch.bfloat16) for _ in range(n)]
@@ -329,7 +364,7 @@ def run_gpu(args):
 
         def one_ep(i, timed=False):
             """``wanferenz_b200.ep.ep_forward`` through the C ABI."""
-            lay = layers[i % len(layers)]
+            lay = lays[i % len(lays)]
             st = L.stream_ptr()
             cfg, wst, ws, wsn = ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(lay.workspace), \
                 lay.workspace.numel()
@@ -363,7 +398,7 @@ def run_gpu(args):
         def one(i, timed=False):
             if world > 1:
                 return one_ep(i, timed)
-            lay = layers[i % len(layers)]
+            lay = lays[i % len(lays)]
             st = L.stream_ptr()
             ev = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in evs[i]])
             args_ = (ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(xs[i]), 0, Tloc,
@@ -379,26 +414,25 @@ def run_gpu(args):
         # the K timed steps as one CUDA graph (NCCL collectives included for N > 1;
         # every rank captures the same sequence), so host launch gaps stay out
         g = torch.cuda.CUDAGraph()
+        n0 = lib.wf_launch_count()
         with torch.cuda.graph(g):
             for i in range(W, n):
                 one(i)
+        launches = int(lib.wf_launch_count() - n0)  # this library's kernels in one replay
         g.replay()  # one untimed replay (graph upload)
         torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
+        t0 = [torch.cuda.Event(enable_timing=True) for _ in range(R)]
+        t1 = [torch.cuda.Event(enable_timing=True) for _ in range(R)]
         with Clocks(local) as clk:
-            t0.record()
-            if g is not None:
+            for r in range(R):
+                barrier()
+                torch.cuda.synchronize()
+                t0[r].record()
                 g.replay()
-            else:
-                for i in range(W, n):
-                    one(i)
-            t1.record()
-            torch.cuda.synchronize()
-        barrier()
-        total_ms = t0.elapsed_time(t1)
+                t1[r].record()
+                torch.cuda.synchronize()
+            barrier()
+        reps = [t0[r].elapsed_time(t1[r]) for r in range(R)]
         # per-kernel durations: eager steps queued behind ~2 ms of copies, so the
         # host runs ahead of the GPU and no launch gap falls inside a kernel's events
         big = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
@@ -420,16 +454,17 @@ def run_gpu(args):
                 kern[k].append(e[j].elapsed_time(e[j + 1]))
         routing = [idx[i].cpu().numpy() for i in range(W, n)]
         del g
-        return total_ms, kern, routing, clk.summary()
+        return reps, kern, routing, clk.summary(), launches
 
-    def stats(Tloc, K, W):
-        total_ms, kern, routing, clk = measure(Tloc, K, W)
-        t = torch.tensor([total_ms], device=dev)
+    def stats(lays, Tloc, K, W, R=1):
+        reps, kern, routing, clk, launches = measure(lays, Tloc, K, W, R)
+        t = torch.tensor(reps, device=dev)
         if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)  # per replay, the slowest rank
+        reps = sorted(float(v) for v in t.tolist())
+        total_ms = reps[len(reps) // 2]  # median replay of K steps
         ms = total_ms / K
-        lay0 = layers[0]
+        lay0 = lays[0]
         if world == 1:
             byts = [step_bytes(r, Tloc, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         else:
@@ -442,24 +477,32 @@ def run_gpu(args):
         tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
                "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
                "max_tokens_per_expert": float(np.mean([h.max() for h in hist]))}
-        return dict(ms=ms, total_ms=total_ms, kms=kms, bytes=mean, layer_bytes=layer_bytes, clocks=clk,
-                    tpe=tpe)
+        return dict(ms=ms, total_ms=total_ms, reps_ms=reps, kms=kms, bytes=mean, layer_bytes=layer_bytes,
+                    clocks=clk, tpe=tpe, launches=launches)
 
-    main = stats(T, args.steps, args.warmup)
+    def summary(r, Tloc):
+        gbs = r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9
+        return {"us_per_step": round(r["ms"] * 1e3, 2), "tokens_per_s": round(Tloc * world / (r["ms"] * 1e-3), 1),
+                "layer_GBps": round(gbs, 1), "layer_frac_of_measured_hbm": round(gbs / hbm, 3),
+                "experts_touched": round(r["bytes"]["experts" if world == 1 else "experts_touched"], 1),
+                "tokens_per_expert": r["tpe"],
+                "kernel_us": {k: round(v * 1e3, 2) for k, v in r["kms"].items()}}
+
+    main = stats(layers, T, args.steps, args.warmup, args.replays)
     sweep = {}
+    extras = {}
     if world == 1:
-        for s in [int(v) for v in args.sweep.split(",") if v]:
-            if s == T:
-                r = main
-            else:
-                r = stats(s, args.steps, args.warmup)
-            layer_gbs = r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9
-            sweep[f"T{s}"] = {
-                "us_per_step": round(r["ms"] * 1e3, 2), "tokens_per_s": round(s / (r["ms"] * 1e-3), 1),
-                "layer_GBps": round(layer_gbs, 1), "layer_frac_of_measured_hbm": round(layer_gbs / hbm, 3),
-                "experts_touched": round(r["bytes"]["experts"], 1),
-                "kernel_us": {k: round(v * 1e3, 2) for k, v in r["kms"].items()},
-            }
+        for s_ in [int(v) for v in args.sweep.split(",") if v]:
+            r = main if s_ == T else stats(layers, s_, args.steps, args.warmup)
+            sweep[f"T{s_}"] = summary(r, s_)
+        if not args.no_extras and args.routing == "uniform":
+            # 64 tokens, Zipf(1.2) popularity, on layers of its own
+            zl = [make_layer(s_, 0, 1, 64, dev, args.init, args.zipf_beta) for s_ in range(args.layers)]
+            extras["config4_T64_zipf"] = summary(stats(zl, 64, args.steps, args.warmup), 64)
+            del zl
+            torch.cuda.empty_cache()
+            # the FP8 block-scaled GEMM at M = 1 and 16
+            extras["config3_fp8_gemm"] = fp8_gemm_points((1, 16), hbm)
     # dominant kernel roofline
     kms = main["kms"]
     # the dominant HBM-bound kernel (multi-GPU: of the compute phases; the collectives
@@ -481,33 +524,21 @@ def run_gpu(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/e4m3 x e4m3 -> f32",
         "data": "synthetic (seeded N(0,0.02) weights quantized like the reference fixtures; N(0,1) bf16 tokens)",
-        "config": {
-            "workload": (f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing"
-                         if args.routing == "uniform" else
-                         f"BASELINE config 4: config-2 layer, {T} tokens per GPU, Zipf(1.2) routing "
-                         f"(gate bias beta={args.zipf_beta})"),
-            "routing": args.routing,
-            "tokens_per_gpu": T, "global_tokens": T * world, "hidden": D, "experts": E, "inter": I,
-            "topk": K_TOP, "layers_cycled": args.layers, "parallelism": f"ep{world}" if world > 1 else "single",
-            "combine": args.combine if world > 1 else None,
-            "l2": f"{args.layers} distinct layers cycled (per-step weights cold in L2), no flush",
-            "timing": "CUDA graph of K steps, CUDA events on the launching stream" if world == 1 else
-                      "CUDA graph of K steps (NCCL collectives captured), CUDA events, max over ranks",
-            "us_per_step": round(main["ms"] * 1e3, 2),
-            "layer_GBps": round(main["layer_bytes"] / (main["ms"] * 1e-3) / 1e9, 1),
-            "kernel_us": {k: round(v * 1e3, 2) for k, v in kms.items()},
-            "experts_touched_per_rank": round(main["bytes"]["experts" if world == 1 else "experts_touched"], 1),
-            "tokens_per_expert": main["tpe"],
-            "sweep": sweep,
-        },
+        "config": workload_config(args, world),
+        "timing": {"method": ("CUDA graph of the K steps" + (" (NCCL collectives captured)" if world > 1 else "") +
+                              ", replayed R times, each replay bracketed by a barrier and a device synchronize "
+                              "and timed with CUDA events on the launching stream; the step time is the median "
+                              "replay / K" + (" (each replay's time the max over ranks)" if world > 1 else "")),
+                   "replays": args.replays, "replay_ms": [round(v, 4) for v in main["reps_ms"]]},
+        "detail": {**summary(main, T), "combine": args.combine if world > 1 else None,
+                   "sweep": sweep, **extras},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / hbm, 4),
                      "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
         "clocks": main["clocks"],
-        # single GPU: K1 + two expert phases; multi-GPU: the router, the same three
-        # on the gathered batch, and the bf16 cast
-        "gpu_launches": 3 * args.steps if world == 1 else 5 * args.steps,
+        # counted: this library's kernels recorded into the graph of the K timed steps
+        "gpu_launches": main["launches"],
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -624,56 +655,53 @@ def cpu_baseline(T):
 
     t = cpu_forward_time(T, reps=2, warmup=1)
     s = float(np.median(t))
-    return {"value": round(T / s, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(T / s, 3), "unit": "tokens/s", "cores": os.cpu_count(), "cpu_model": cpu_model(),
+            "kind": "port",
             "sample": f"config-2 layer forwards of {T} tokens (median of 2 after 1 warm-up) by the torch "
                       f"CPU restatement of the reference's path (oracle/torch_port.py: the reference's "
                       f"ops, fp32 BLAS, {os.cpu_count()} host threads); {s:.2f} s each"}
 
 
 def run_reference(args):
-    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+    """--impl reference: the reference algorithm (the torch restatement of its CPU path)
+    on the host cores, every step a forward of all ``--tokens`` tokens of the workload."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     T = args.tokens
-    # each step a bounded sample of the workload: 4 of its tokens (~2.3 s on 8 cores)
-    sample = min(T, 4)
-    cpu_forward_time(sample, reps=0, warmup=max(args.warmup, 1), seed=1)
-    times = cpu_forward_time(sample, reps=args.steps, seed=2)
+    cpu_forward_time(T, reps=0, warmup=max(args.warmup, 1), seed=1)
+    times = cpu_forward_time(T, reps=args.steps, seed=2)
     s = sum(times) / len(times)
-    value = sample / s
+    value = T / s
+    sample = (f"all {T} tokens of each step through the torch CPU restatement of the reference's "
+              f"MoE.forward (oracle/torch_port.py; the reference's ops, fp32 BLAS, "
+              f"{os.cpu_count()} host threads on {cpu_model()})")
     out = {
         "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(s * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"BASELINE config 2: V4-Flash MoE decode layer, {T} tokens per GPU, uniform routing",
-                   "tokens_per_gpu": T, "sample_tokens_per_step": sample},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": os.cpu_count(),
-                         "kind": "port",
-                         "sample": f"{sample} of the {T} tokens per step through the torch CPU restatement "
-                                   f"of the reference's MoE.forward (oracle/torch_port.py; the reference's "
-                                   f"ops, fp32 BLAS, all host threads)"},
+                         "cpu_model": cpu_model(), "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
 
 
-def run_fp8_gemm_suite(args):
+def fp8_gemm_points(Ms, hbm):
     """``fp8_gemm`` (architecture.py:121-134 -> torch_ops.py:93-99) for
-    M in {1, 2, 4, 8, 16} and the four (N, K) of the model's dense projections, E4M3
-    weights with one fp32 (config 3) or e8m0 (model path) scale per 128x128 block,
-    bf16 activations quantized per token (1x128 fp32 scales).  Each point: R calls
-    cycling enough weight copies to exceed L2, captured in a CUDA graph, replayed and
-    timed with CUDA events.  Bytes per call: N*K + scales + M*K*2 + M*N*2."""
+    the M in ``Ms`` and the four (N, K) of the model's dense projections, E4M3 weights
+    with one fp32 (config 3) or e8m0 (model path) scale per 128x128 block, bf16
+    activations quantized per token (1x128 scales).  Each point: R calls cycling
+    enough weight copies to exceed L2, captured in a CUDA graph, replayed and timed
+    with CUDA events.  Bytes per call: N*K + scales + M*K*2 + M*N*2."""
     import torch
 
     from wanferenz_b200 import ops
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    hbm, peak_kind = peaks()
+    dev = torch.device("cuda", torch.cuda.current_device())
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     res = []
@@ -688,7 +716,7 @@ def run_fp8_gemm_suite(args):
         # f32: config 3 as stated (fp32 scales on both sides); e8m0: the model path
         # (scale_fmt="ue8m0", e8m0 scales on both sides, architecture.py:121-134)
         for kind, bs in (("f32", s32), ("e8m0", s8.view(torch.float8_e8m0fnu))):
-            for M in (1, 2, 4, 8, 16):
+            for M in Ms:
                 x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
                 if kind == "f32":
                     aq, a_s = ops.act_quant(x, 128)
@@ -720,6 +748,16 @@ def run_fp8_gemm_suite(args):
                             "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
         del wqs, wq, q, s8, s32
         torch.cuda.empty_cache()
+    return res
+
+
+def run_fp8_gemm_suite(args):
+    """``--suite fp8_gemm``: the whole config-3 sweep, M in {1, 2, 4, 8, 16}, one JSON line."""
+    import torch
+
+    torch.cuda.set_device(0)
+    hbm, peak_kind = peaks()
+    res = fp8_gemm_points((1, 2, 4, 8, 16), hbm)
     out = {"suite": "fp8_gemm", "metric": "FP8 block-scaled GEMM us/call (BASELINE config 3)",
            "unit": "us", "higher_is_better": False, "peak_GBps": hbm, "peak_kind": peak_kind,
            "timing": "CUDA graph of R calls over weight copies > L2, CUDA events", "results": res}

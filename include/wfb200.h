@@ -7,8 +7,9 @@
  * Every entry point returns an int status (WF_OK or a negative WF_E_* code);
  * wf_last_error() returns the message of the last failure on the calling
  * host thread.  No entry point allocates device memory, synchronizes the
- * stream or reads device data back, except the load-time checks
- * wf_fp4_scales_in_range() and wf_moe_read_error(), which say so.
+ * stream or reads device data back, except the load-time check
+ * wf_fp4_scales_in_range() and the error-word reads wf_moe_read_error() and
+ * wf_moe_read_error_noalloc(), which say so.
  *
  * Data formats (identical to the reference's tensors, so a reference
  * checkpoint's bytes are passed through unchanged):
@@ -133,17 +134,29 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
  * (cudaMalloc may synchronize the whole device).  The caller passes inputs and
  * outputs only; the scratch is a 4 MiB array in this library's device module
  * (WF_NOALLOC_SCRATCH_BYTES), which every device that loads the library keeps
- * until the process exits.  A T whose scratch would exceed it (about 48 tokens
- * at the V4-Flash shapes) is rejected with WF_E_SHAPE.  The first call on a
- * device looks the array's device address up (cudaGetSymbolAddress); make that
- * first call before any stream capture.  Each call zeroes the array's counters
- * (a cudaMemsetAsync on `stream`) and calls no allocator.  All calls on a
- * device share the one array and it keeps the last call's contents, so calls
- * that overlap on the GPU (other streams, other threads) race: order them on
- * one stream.  No counterpart in the reference. */
+ * until the process exits.  A T whose scratch would exceed it is rejected with
+ * WF_E_SHAPE before anything runs: at the V4-Flash shapes (hidden 4096, inter
+ * 2048, 256 experts, top-6) the limit is T = 48, at hidden 2048 / inter 1024 /
+ * 64 experts it is T = 96.  The expert phases run on the mma.sync engine.
+ * The first call in a device's context looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Each call clears the array's completion counters (a cudaMemsetAsync on
+ * `stream`) and calls no allocator.  The array's error word is not cleared:
+ * it collects the flags of every call (an out-of-range token or expert id, a
+ * timed-out device wait) until wf_moe_read_error_noalloc reads and clears it.
+ * All calls on a device share the one array and it keeps the last call's
+ * contents, so calls that overlap on the GPU (other streams, other threads)
+ * race: order them on one stream.  No counterpart in the reference. */
 int wf_moe_forward_noalloc(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
                            const int64_t *input_ids, int32_t T, void *y, float *out_weights,
                            int64_t *out_indices, void *stream);
+
+/* wf_moe_read_error for wf_moe_forward_noalloc: copies the static scratch's
+ * error word to the host (synchronizes `stream`) and clears it; returns 0 or
+ * the WF_E_* code of a flag set by any allocation-free call since the last
+ * read (a timed-out device wait first).  Allocates nothing.  No counterpart in
+ * the reference. */
+int wf_moe_read_error_noalloc(void *stream);
 
 /* Expert-parallel forward on a gathered batch with its routing given.  The
  * reference (MoE.forward, architecture.py:749-756, 785-794) has every rank
@@ -194,6 +207,22 @@ int wf_moe_route(const wf_moe_config *cfg, const wf_moe_weights *w, const void *
  * workspace since it was last read; returns 0 or the negative WF_E_* code of
  * a flag that is set (a timed-out device wait first). */
 int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bound, in SM clock cycles, of the layer kernels' waits on another role's
+ * progress (a pipeline stage, an operand, an accumulator) for launches made
+ * after this call, process-wide; cycles <= 0 restores the default (2e9 cycles,
+ * about a second).  A wait that runs past it sets WF_E_TIMEOUT in the error
+ * word and the kernel winds down: waits for the calling thread's own copies
+ * and MMAs keep the default bound, so no CTA exits or frees tensor memory
+ * with work in flight, and the context stays usable.  A failure-detection
+ * hook (tests lower it so that a wait runs out); no counterpart in the
+ * reference, whose waits are the host's (serving/chain.py:276-316). */
+int wf_set_wait_limit(int64_t cycles);
+
+/* Number of kernels this library has launched in this process, counting a
+ * launch recorded into a stream capture once (measurement: the kernels a
+ * timed region runs).  No counterpart in the reference. */
+uint64_t wf_launch_count(void);
 
 /* act_quant (wanferenz/kernels/torch_ops.py:33-49; TileLang reference.py:117-146):
  * x [M, K] bf16 -> q [M, K] e4m3 and s [M, K/block] scales of `scale_kind`.

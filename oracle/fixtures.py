@@ -13,7 +13,11 @@ tensor can be regenerated bit-exactly, one expert at a time, on any machine:
   ``fp4_act_quant`` (packed E2M1 + e8m0 per 32 along K);
 * shared expert: w1, w3 ``[I, D]``, w2 ``[D, I]`` N(0, 0.02) bf16 ->
   ``fp8_block_quant`` (e4m3 + e8m0 per 128x128);
-* activations ``[T, D]`` N(0, 1) bf16.
+* activations ``[T, D]`` N(0, 1) bf16;
+* optional Zipf expert popularity: over a seeded
+  permutation giving each expert a popularity rank r in 1..E, the gate bias
+  gets ``zipf_beta * log(r ** -zipf)`` added, so expert popularity falls off
+  like a Zipf(zipf) law (many experts get no token, a few get more than 16).
 """
 
 from __future__ import annotations
@@ -27,6 +31,7 @@ from . import moe_oracle as O
 
 TAG_GATE_W, TAG_GATE_B, TAG_W1, TAG_W3, TAG_W2 = 1, 2, 3, 4, 5
 TAG_SW1, TAG_SW3, TAG_SW2, TAG_X, TAG_TID2EID, TAG_IDS = 6, 7, 8, 9, 10, 11
+TAG_ZIPF = 12
 
 
 def rng(*key: int) -> np.random.Generator:
@@ -64,6 +69,8 @@ class LayerSpec:
     seed: int = 0
     ue8m0: bool = True
     hash_pattern: tuple = ()
+    zipf: float = 0.0        # Zipf exponent of the expert popularity bias (0: uniform routing)
+    zipf_beta: float = 0.08  # bias scale of the Zipf recipe
 
     def as_dict(self):
         return dataclasses.asdict(self)
@@ -72,6 +79,16 @@ class LayerSpec:
 # BASELINE.json configs 1 and 2 (config 2 at the real V4-Flash shapes)
 CONFIG1 = LayerSpec(D=2048, I=1024, E=64, topk=6, score_func="sigmoid", route_scale=1.5)
 CONFIG2 = LayerSpec(D=4096, I=2048, E=256, topk=6, score_func="sigmoid", route_scale=1.5)
+# the config-2 layer with Zipf(1.2) expert popularity
+CONFIG4 = LayerSpec(D=4096, I=2048, E=256, topk=6, score_func="sigmoid", route_scale=1.5, zipf=1.2)
+
+
+def zipf_bias(seed: int, E: int, s: float, beta: float) -> np.ndarray:
+    """``beta * log(rank_e ** -s)`` for a seeded popularity rank ``rank_e`` in 1..E."""
+    perm = rng(seed, TAG_ZIPF).permutation(E)
+    rank = np.empty(E, np.float32)
+    rank[perm] = np.arange(1, E + 1, dtype=np.float32)
+    return (np.float32(beta) * np.log(rank ** np.float32(-s))).astype(np.float32)
 
 
 class SyntheticLayer:
@@ -92,16 +109,21 @@ class SyntheticLayer:
         else:
             self.gate_b = (rng(s.seed, TAG_GATE_B).standard_normal(s.E, dtype=np.float32)
                            * np.float32(s.bias_std)).astype(np.float32)
+            if s.zipf:
+                self.gate_b = (self.gate_b + zipf_bias(s.seed, s.E, s.zipf, s.zipf_beta)).astype(np.float32)
             self.tid2eid = None
         self._experts = {}
         self._shared = None
 
     # -- raw bf16 sources -------------------------------------------------
-    def expert_bf16(self, e):
-        s = self.spec
+    @staticmethod
+    def _sources(s: LayerSpec, e: int):
         return (normal_bf16((s.seed, TAG_W1, e), (s.I, s.D), s.w_std),
                 normal_bf16((s.seed, TAG_W3, e), (s.I, s.D), s.w_std),
                 normal_bf16((s.seed, TAG_W2, e), (s.D, s.I), s.w_std))
+
+    def expert_bf16(self, e):
+        return self._sources(self.spec, e)
 
     def shared_bf16(self):
         s = self.spec

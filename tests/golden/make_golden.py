@@ -43,7 +43,10 @@ from oracle import fixtures as F  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
 
 # Layer cases: name -> (spec, T values).  Small "mini" shapes cover each
-# routing / activation option; cfg1 and cfg2 are BASELINE configs 1 and 2.
+# routing / activation option; cfg1 and cfg2 are BASELINE configs 1 and 2;
+# cfg2_batch is config 2 at the benchmark's 16 tokens and cfg4 is BASELINE
+# config 4 (64 tokens, Zipf(1.2) expert popularity: experts with more than 16
+# tokens, i.e. several token groups of one expert).
 LAYER_CASES = {
     "mini_sigmoid": (F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="sigmoid",
                                  route_scale=1.5, seed=11), (1, 5)),
@@ -61,6 +64,8 @@ LAYER_CASES = {
                                    route_scale=1.5, ue8m0=False, seed=16), (3,)),
     "cfg1": (F.CONFIG1, (1, 8)),
     "cfg2": (F.CONFIG2, (1, 4)),
+    "cfg2_batch": (F.CONFIG2, (16,)),
+    "cfg4": (F.CONFIG4, (64,)),
 }
 
 

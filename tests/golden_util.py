@@ -27,4 +27,4 @@ def spec_of(case):
 
 
 LAYER_FILES = ("mini_sigmoid", "mini_sqrtsoftplus_clamp", "mini_softmax", "mini_hash_dups",
-               "mini_hash_random", "mini_fp32scale", "cfg1", "cfg2")
+               "mini_hash_random", "mini_fp32scale", "cfg1", "cfg2", "cfg2_batch", "cfg4")

@@ -24,18 +24,23 @@ SPEC = F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="sigmoid", route_scale
 
 
 class OracleShard:
-    """CPU stand-in with MoELayer's route / forward_ep / to_bf16 contract."""
+    """CPU stand-in with MoELayer's route / forward_ep / to_bf16 contract, including
+    its capacity: at most ``max_tokens`` rows per call (the workspace's size)."""
 
-    def __init__(self, syn, lo, hi):
-        self.syn, self.lo, self.hi = syn, lo, hi
+    def __init__(self, syn, lo, hi, max_tokens=64):
+        self.syn, self.lo, self.hi, self.max_tokens = syn, lo, hi, max_tokens
 
     def route(self, x, input_ids=None):
+        assert x.size(0) <= self.max_tokens, "route: more rows than the workspace holds"
         p = self.syn.params()
         w, idx, _ = O.gate(x.float().numpy(), p["gate_w"], p.get("gate_b"), p["topk"], p["score_func"],
                            p["route_scale"], p.get("tid2eid"), input_ids)
         return torch.from_numpy(w), torch.from_numpy(idx)
 
     def forward_ep(self, x, weights, indices, shared_rows=(0, 0)):
+        assert x.size(0) <= self.max_tokens, "forward_ep: more rows than the workspace holds"
+        r0, n = shared_rows
+        assert 0 <= r0 and r0 + n <= x.size(0), "shared rows outside the batch"
         xf = x.float().numpy()
         p, _, _ = O.moe_forward(xf, self.syn.params(), None, expert_range=(self.lo, self.hi),
                                 return_partial=True, routing=(weights.numpy(), indices.numpy()))
@@ -62,7 +67,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, T, q, combine="reduce_scatter"):
+def _worker(rank, world, port, T, q, combine="reduce_scatter", max_tokens=64):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -73,20 +78,22 @@ def _worker(rank, world, port, T, q, combine="reduce_scatter"):
         x = torch.from_numpy(O.bf16_to_f32(x16)).to(torch.bfloat16)
         mine = x[rank * T:(rank + 1) * T]
         lo, hi = shard_range(SPEC.E, world, rank)
-        y = ep_forward(OracleShard(syn, lo, hi), mine, combine=combine)
+        y = ep_forward(OracleShard(syn, lo, hi, max_tokens), mine, combine=combine)
         q.put((rank, y.float().numpy()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,T,combine", [(2, 1, "reduce_scatter"), (2, 3, "reduce_scatter"),
-                                             (2, 3, "all_to_all"), (4, 2, "reduce_scatter"),
-                                             (4, 2, "all_to_all")])
-def test_ep_forward_matches_single_process(world, T, combine):
+@pytest.mark.parametrize("world,T,combine,cap", [(2, 1, "reduce_scatter", 64), (2, 3, "reduce_scatter", 64),
+                                                 (2, 3, "all_to_all", 64), (4, 2, "reduce_scatter", 64),
+                                                 (4, 2, "all_to_all", 64),
+                                                 # gathered batch (P*T) above the workspace capacity: pieces
+                                                 (2, 5, "reduce_scatter", 4), (4, 3, "all_to_all", 5)])
+def test_ep_forward_matches_single_process(world, T, combine, cap):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, q, combine)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, q, combine, cap)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=180) for _ in range(world))

@@ -36,31 +36,45 @@ def _syn(spec):
 
 
 def _layer(spec, touched, **kw):
-    key = (spec, tuple(sorted(touched)), tuple(sorted(kw.items())))
+    """Device layers are cached (a few at a time) so both engines reuse one upload."""
+    key = (spec, tuple(sorted(int(e) for e in touched)),
+           tuple(sorted((k, v) for k, v in kw.items() if k not in ("expert_sha", "shared_sha"))))
     if key not in _LAYERS:
-        _LAYERS.clear()
+        while len(_LAYERS) >= 3:
+            _LAYERS.pop(next(iter(_LAYERS)))
         torch.cuda.empty_cache()
         _LAYERS[key] = U.device_layer(_syn(spec), touched, **kw)
     return _LAYERS[key]
 
 
+@pytest.fixture(params=["tcgen05", "mma_sync"])
+def engine(request, monkeypatch):
+    """Both expert engines: tcgen05 (default where scales are e8m0) and the mma.sync one."""
+    monkeypatch.setenv("WF_DISABLE_TC", "0" if request.param == "tcgen05" else "1")
+    return request.param
+
+
 @pytest.mark.parametrize("name,key", list(_golden_cases()))
-def test_layer_matches_reference_golden(name, key):
+def test_layer_matches_reference_golden(name, key, engine):
+    """Every token of every golden case (up to config 4's 64 tokens with Zipf routing)
+    against the reference's own outputs, on weights whose quantized bytes are checked
+    against the reference's (sha256)."""
     case = G.load(name)[key]
     spec = G.spec_of(case)
     T = int(case["T"])
     syn = _syn(spec)
     x16, ids = syn.activations(T)
     touched = np.unique(case["indices"])
-    dl = _layer(spec, touched)
+    sha = {int(e): str(h) for e, h in zip(case["expert_ids"], case["expert_sha"])}
+    dl = _layer(spec, touched, max_tokens=max(64, T), expert_sha=sha, shared_sha=str(case["shared_sha"]))
     x = U.bf16_tensor(x16)
     y, rw, ri = dl.forward(x, torch.from_numpy(ids).cuda(), routing=True)
     torch.cuda.synchronize()
     dl.read_error()
-    tie = U.near_tie_rows(O.bf16_to_f32(x16), syn)
+    tie = U.near_tie_rows_from_logits(case["logits"], syn, what=f"{key} {engine}")
     np.testing.assert_array_equal(ri.cpu().numpy()[~tie], case["indices"][~tie])
     np.testing.assert_allclose(rw.cpu().numpy()[~tie], case["weights"][~tie], rtol=2e-6, atol=1e-7)
-    U.assert_layer_close(U.to_f32(y)[~tie], O.bf16_to_f32(case["y"])[~tie], key)
+    U.assert_layer_close(U.to_f32(y)[~tie], O.bf16_to_f32(case["y"])[~tie], f"{key} {engine}")
 
 
 ORACLE_SPECS = [
@@ -72,13 +86,6 @@ ORACLE_SPECS = [
     F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="sigmoid", ue8m0=False, seed=25),
     F.CONFIG1,
 ]
-
-
-@pytest.fixture(params=["tcgen05", "mma_sync"])
-def engine(request, monkeypatch):
-    """Both expert engines: tcgen05 (default where scales are e8m0) and the mma.sync one."""
-    monkeypatch.setenv("WF_DISABLE_TC", "0" if request.param == "tcgen05" else "1")
-    return request.param
 
 
 @pytest.mark.parametrize("spec", ORACLE_SPECS, ids=lambda s: f"D{s.D}_E{s.E}_{s.score_func}_h{int(s.hash_layer)}_u{int(s.ue8m0)}")
@@ -98,6 +105,51 @@ def test_layer_matches_oracle(spec, T, engine):
     tie = U.near_tie_rows(x, syn)
     np.testing.assert_array_equal(ri.cpu().numpy()[~tie], i_ref[~tie])
     U.assert_layer_close_envelope(U.to_f32(y)[~tie], y_ref[~tie], y_ref32[~tie], f"T={T}")
+
+
+_PORT_REF = {}
+
+
+@pytest.mark.parametrize("spec", [F.CONFIG2, F.CONFIG4], ids=["uniform", "zipf"])
+def test_prefill_256_tokens_against_torch_port(spec, engine):
+    """A config-5-sized layer step: 256 tokens at the V4-Flash shapes, uniform and
+    Zipf(1.2) routing, every token against the torch CPU restatement of the
+    reference's path (oracle/torch_port.py, pinned to the reference's golden
+    vectors).  All 256 experts hold seeded random FP4 bytes; the shared expert is
+    the fixture's."""
+    import os
+
+    from oracle import torch_port as P
+
+    syn = _syn(spec)
+    T = 256
+    x16, _ = syn.activations(T, draw=9)
+    xf = O.bf16_to_f32(x16)
+    dl = _layer(spec, [], max_tokens=T)
+    key = (spec, T)
+    if key not in _PORT_REF:
+        torch.set_num_threads(os.cpu_count() or 1)
+        w, I = dl.weights, spec.I
+
+        def experts(e):
+            return tuple(t.cpu().numpy() for t in (w.w13[e, :I], w.w13_s[e, :I], w.w13[e, I:], w.w13_s[e, I:],
+                                                   w.w2[e], w.w2_s[e]))
+
+        p = syn.params()
+        p["experts"] = experts
+        wr, ir = P.gate(P._t(xf), p)
+        _PORT_REF[key] = (P.moe_forward(xf, p).numpy(), wr.numpy(), ir.numpy())
+    y_ref, w_ref, i_ref = _PORT_REF[key]
+    counts = np.bincount(i_ref.ravel(), minlength=spec.E)
+    if spec.zipf:
+        assert counts.max() > 32, "Zipf routing should give experts several token groups"
+    y, rw, ri = dl.forward(U.bf16_tensor(x16), routing=True)
+    torch.cuda.synchronize()
+    dl.read_error()
+    tie = U.near_tie_rows(xf, syn, what=f"T=256 {'zipf' if spec.zipf else 'uniform'} {engine}")
+    np.testing.assert_array_equal(ri.cpu().numpy()[~tie], i_ref[~tie])
+    np.testing.assert_allclose(rw.cpu().numpy()[~tie], w_ref[~tie], rtol=1e-5, atol=1e-7)
+    U.assert_layer_close(U.to_f32(y)[~tie], y_ref[~tie], f"T=256 {engine}")
 
 
 def test_hash_duplicates_keep_one_contribution():

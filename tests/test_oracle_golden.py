@@ -94,6 +94,36 @@ def test_oracle_operator_goldens():
     assert np.array_equal(O.f32_to_bf16(c4), ops["op_fp4_gemm"]["c"])
 
 
+@pytest.mark.parametrize("name,key", [("cfg2_batch", "cfg2_batch_T16"), ("cfg4", "cfg4_T64")])
+def test_oracle_router_matches_reference_full_batch(name, key):
+    """The full-batch golden cases (the benchmark's 16 tokens; config 4's 64 tokens
+    with Zipf popularity): the oracle's router (gate bias recipe included) gives the
+    reference's logits, indices and weights.  Their layer outputs are checked on the
+    GPU against the reference's, on weights pinned to the reference's bytes."""
+    case = G.load(name)[key]
+    spec = G.spec_of(case)
+    layer = F.SyntheticLayer(spec)
+    x16, ids = layer.activations(int(case["T"]))
+    x = O.bf16_to_f32(x16)
+    logits, _ = O.gate_scores(x, layer.gate_w, spec.score_func)
+    np.testing.assert_allclose(logits, case["logits"], rtol=0, atol=2e-6)
+    w, idx, biased = O.gate(x, layer.gate_w, layer.gate_b, spec.topk, spec.score_func, spec.route_scale)
+    tie = O.topk_margin(biased, spec.topk) < 1e-6
+    assert tie.sum() <= max(1, len(tie) // 64)
+    np.testing.assert_array_equal(idx[~tie], case["indices"][~tie])
+    np.testing.assert_allclose(w[~tie], case["weights"][~tie], rtol=1e-6, atol=1e-7)
+
+
+def test_config4_golden_has_multi_group_experts():
+    """The config-4 golden case exercises experts with more than 16 tokens (several
+    16-token groups of one expert, i.e. B-operand reloads at K = 4096 / 2048) and
+    many experts with none."""
+    case = G.load("cfg4")["cfg4_T64"]
+    counts = np.bincount(case["indices"].ravel(), minlength=256)
+    assert (counts > 16).sum() >= 2 and counts.max() > 32
+    assert (counts == 0).sum() > 128
+
+
 def test_planted_mistake_is_caught():
     """A deliberately wrong oracle (bias dropped) must disagree with the golden indices."""
     case = G.load("mini_sigmoid")["mini_sigmoid_T5"]

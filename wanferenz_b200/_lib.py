@@ -24,7 +24,8 @@ EXPORTS = (
     "wf_moe_finish", "wf_moe_route", "wf_moe_read_error", "wf_act_quant", "wf_fp4_act_quant",
     "wf_fp8_gemm", "wf_fp4_gemm", "wf_grouped_fp4_gemm", "wf_gemm_workspace_bytes",
     "wf_fp4_scales_in_range", "wf_moe_forward_noalloc", "wf_moe_forward_ep", "wf_moe_to_bf16",
-    "wf_moe_sum_ranks",
+    "wf_moe_sum_ranks", "wf_moe_read_error_noalloc", "wf_set_wait_limit",
+    "wf_launch_count",
 )
 
 
@@ -88,6 +89,9 @@ def _declare(lib):
         "wf_fp4_scales_in_range": (ctypes.c_int, [P, I64, P]),
         "wf_moe_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights),
                                                   P, P, I32, P, P, P, P]),
+        "wf_moe_read_error_noalloc": (ctypes.c_int, [P]),
+        "wf_set_wait_limit": (ctypes.c_int, [I64]),
+        "wf_launch_count": (ctypes.c_uint64, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

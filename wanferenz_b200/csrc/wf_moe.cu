@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -115,6 +116,8 @@ struct MoeArgs {
     // rows to the output (whole layer: all rows; partial forward: none, wf_moe_finish
     // adds them; expert-parallel: the rank's own rows of the gathered batch)
     int sh0, shT, sh_add;
+    // bound (SM cycles) of waits on another role's progress (wf_set_wait_limit)
+    long long wait_limit;
 };
 
 // Dense GEMM (operator entry points) arguments.
@@ -330,17 +333,18 @@ __device__ __forceinline__ void item_range(int n, int &i0, int &i1) {
 // producer: stream each item's weight rows (and FP4 scales) into the ring
 // ---------------------------------------------------------------------------
 template <typename Decode>
-__device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode) {
+__device__ void produce(const Smem &sm, int i0, int i1, int *err, long long lim, Decode decode) {
     if ((threadIdx.x & 31) != 0) return;
     volatile int *abort = sm.flags();
-    int q = 0;
+    int q = 0, armed = 0;  // items walked; items whose copies were issued (a prefix)
     for (int i = i0; i < i1; ++i, ++q) {
         const Item it = decode(i);
         const int s = q % NSLOT;
         if (q >= NSLOT && !*abort) {
-            if (!wf_wait(sm.empty(s), ((q / NSLOT) - 1) & 1, err)) *abort = 1;
+            if (!wf_wait(sm.empty(s), ((q / NSLOT) - 1) & 1, err, lim)) *abort = 1;
         }
         if (*abort) continue;
+        ++armed;
         const uint32_t rowb = it.fmt == FMT_FP4 ? it.K / 2 : it.K;
         const uint32_t ks = it.K / 32;
         const int na = it.nrun * it.rrows;
@@ -366,8 +370,9 @@ __device__ void produce(const Smem &sm, int i0, int i1, int *err, Decode decode)
             }
         }
     }
-    // drain: every armed phase must complete before the CTA may exit
-    const int nq = q;
+    // drain: every armed phase must complete before the CTA may exit (after an
+    // abort only the first `armed` items were issued)
+    const int nq = armed;
     for (int s = 0; s < NSLOT && s < nq; ++s) {
         const int last = s + ((nq - 1 - s) / NSLOT) * NSLOT;
         wf_wait(sm.full(s), (last / NSLOT) & 1, err);
@@ -630,7 +635,7 @@ __device__ __forceinline__ float swiglu(float gv, float uv, float limit) {
 // Generic consumer loop.  `epi(it, red, tid)` runs on the 256 consumer
 // threads after the fixed-order cross-warp reduction inputs are in `red`.
 template <typename Decode, typename RowPtr, typename PreqScale, typename FP8Scale, typename Epi>
-__device__ void consume(const Smem &sm, int i0, int i1, int ue8m0, int *err, Decode decode,
+__device__ void consume(const Smem &sm, int i0, int i1, int ue8m0, int *err, long long lim, Decode decode,
                         RowPtr rowptr, PreqScale preq_scale, FP8Scale f8s, Epi epi) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tig = lane & 3;
@@ -647,7 +652,7 @@ __device__ void consume(const Smem &sm, int i0, int i1, int ue8m0, int *err, Dec
             key_src = it.bsrc; key_tok0 = it.tok0; key_ntok = it.ntok; key_a = it.a;
         }
         bool ok = !*abort;
-        if (ok && !wf_wait(sm.full(s), (q / NSLOT) & 1, err)) { *abort = 1; ok = false; }
+        if (ok && !wf_wait(sm.full(s), (q / NSLOT) & 1, err, lim)) { *abort = 1; ok = false; }
         float acc[2][NTM][4];
 #pragma unroll
         for (int m = 0; m < 2; ++m)
@@ -1271,7 +1276,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
             }
             return;
         }
-        produce(sm, i0, i1, a.err, decode);
+        produce(sm, i0, i1, a.err, a.wait_limit, decode);
         return;
     }
     if (given) {
@@ -1312,7 +1317,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
             a.hs[(size_t)(it.tok0 + tok) * a.I + it.row0 + j] = __float2bfloat16_rn(hv);
         }
     };
-    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+    consume(sm, i0, i1, a.ue8m0, a.err, a.wait_limit, decode, rp, NoPreq{}, f8, epi);
 }
 
 __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ MoeArgs a) {
@@ -1335,7 +1340,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
         return decode_moe(KID_MID, a, i, c.ai, n_it2, rt.act_expert, rt.act_off, rt.act_it);
     };
     if ((threadIdx.x >> 5) == NCW) {
-        produce(sm, i0, i1, a.err, decode);
+        produce(sm, i0, i1, a.err, a.wait_limit, decode);
         return;
     }
     MoeRowPtr rp{&a, rt.pair_tok};
@@ -1363,7 +1368,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_mid(const __grid_constant__ Moe
             }
         }
     };
-    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+    consume(sm, i0, i1, a.ue8m0, a.err, a.wait_limit, decode, rp, NoPreq{}, f8, epi);
 }
 
 __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ MoeArgs a) {
@@ -1389,7 +1394,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ Mo
         return decode_moe(KID_DOWN, a, i, c.ai, 0, rt.act_expert, rt.act_off, rt.act_it);
     };
     if ((threadIdx.x >> 5) == NCW) {
-        produce(sm, i0, i1, a.err, decode);
+        produce(sm, i0, i1, a.err, a.wait_limit, decode);
         return;
     }
     MoeRowPtr rp{&a, rt.pair_tok};
@@ -1414,7 +1419,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_down(const __grid_constant__ Mo
             if (tid == 0) a.cnt_rb[it.rb] = 0u;
         }
     };
-    consume(sm, i0, i1, a.ue8m0, a.err, decode, rp, NoPreq{}, f8, epi);
+    consume(sm, i0, i1, a.ue8m0, a.err, a.wait_limit, decode, rp, NoPreq{}, f8, epi);
 }
 
 __global__ void k_moe_finish(const float *yp, const __nv_bfloat16 *os, __nv_bfloat16 *y, int n) {
@@ -1455,7 +1460,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ Dense
     item_range(n, i0, i1);
     auto decode = [&](int i) { return decode_dense(d, i); };
     if ((threadIdx.x >> 5) == NCW) {
-        produce(sm, i0, i1, d.err, decode);
+        produce(sm, i0, i1, d.err, kWaitLimitCycles, decode);
         return;
     }
     auto rowptr = [&](const Item &it, int j) -> const void * {
@@ -1501,7 +1506,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ Dense
             if (tid == 0) d.cnt[it.rb] = 0u;
         }
     };
-    consume(sm, i0, i1, 1, d.err, decode, rowptr, preq, f8, epi);
+    consume(sm, i0, i1, 1, d.err, kWaitLimitCycles, decode, rowptr, preq, f8, epi);
 }
 
 // ---- standalone quantizers --------------------------------------------------
@@ -1711,6 +1716,13 @@ int cached_map(CUtensorMap *out, bool fp4, int rank, const void *base, const uin
     return WF_OK;
 }
 
+// Bound of the kernels' waits on another role's progress; wf_set_wait_limit lowers it.
+std::atomic<long long> g_wait_limit{wf::kWaitLimitCycles};
+
+// Kernels this library has launched (or recorded into a stream capture) in this process.
+std::atomic<unsigned long long> g_launches{0};
+inline void counted(int n = 1) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
 bool tc_disabled() {
     const char *v = getenv("WF_DISABLE_TC");
     return v && v[0] && v[0] != '0';
@@ -1745,7 +1757,9 @@ size_t tc_max_items(const wf_moe_config *c) {
     return groups * std::max<size_t>(nblk, 1);
 }
 
-WsLayout ws_layout(const wf_moe_config *c) {
+// tc_counters = false: the layout of the allocation-free forward, which never runs
+// the tcgen05 phases and so leaves out their per-item counters.
+WsLayout ws_layout(const wf_moe_config *c, bool tc_counters = true) {
     WsLayout L{};
     size_t off = 0;
     const size_t T = c->max_tokens, K = c->topk, E = c->n_experts, El = c->n_local_experts;
@@ -1757,7 +1771,7 @@ WsLayout ws_layout(const wf_moe_config *c) {
     L.err = take(16);
     L.cnt_router = take(16);
     L.cnt_rb = take((size_t)(c->dim / 8 + 1) * 4);
-    L.cnt_tc = take(tc_max_items(c) * 4);
+    L.cnt_tc = take(tc_counters ? tc_max_items(c) * 4 : 0);
     L.hdr = take(wf::H_SIZE * 4);
     L.logits = take(T * E * 4);
     L.act_expert = take((El + 1) * 4);
@@ -1882,12 +1896,12 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
 
 int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
               const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a,
-              wf::mtc::TcArgs *t = nullptr, bool routing_given = false) {
+              wf::mtc::TcArgs *t = nullptr, bool routing_given = false, bool tc_counters = true) {
     int rc = check_cfg(c);
     if (rc) return rc;
     if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
     if (T <= 0 || T > c->max_tokens) return fail(WF_E_SHAPE, "T outside 1..max_tokens");
-    const WsLayout L = ws_layout(c);
+    const WsLayout L = ws_layout(c, tc_counters);
     if (ws_bytes < L.total) return fail(WF_E_ARG, "workspace too small");
     if (!w->gate_w) return fail(WF_E_ARG, "null gate weight");
     if (c->hash_layer && !routing_given && (!w->tid2eid || !ids))
@@ -1948,6 +1962,7 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
     int G = sm_count();
     if (G <= 0) return fail(WF_E_CUDA, "no CUDA device");
     a.route_only = route_only;
+    a.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
     if (a.tc && !t) return fail(WF_E_ARG, "tcgen05 phases without their arguments");
     // Programmatic dependent launch: a kernel may begin launching while the one
     // before it drains; each kernel waits (griddepcontrol.wait) before reading
@@ -1973,18 +1988,18 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
             e = cudaEventRecordWithFlags((cudaEvent_t)ev[i], st, cudaEventRecordDefault);
     };
     rec(0);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_up, a);
+    if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lc, wf::k_moe_up, a)) == cudaSuccess) counted();
     rec(1);
     if (!route_only) {
         if (a.tc) {
-            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<2>, a, *t);
+            if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<2>, a, *t)) == cudaSuccess) counted();
             rec(2);
-            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<3>, a, *t);
+            if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lt, wf::mtc::k_moe_tc<3>, a, *t)) == cudaSuccess) counted();
             rec(3);
         } else {
-            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_mid, a);
+            if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lc, wf::k_moe_mid, a)) == cudaSuccess) counted();
             rec(2);
-            if (e == cudaSuccess) e = cudaLaunchKernelEx(&lc, wf::k_moe_down, a);
+            if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lc, wf::k_moe_down, a)) == cudaSuccess) counted();
             rec(3);
         }
     }
@@ -2066,7 +2081,7 @@ int wf_moe_sum_ranks(const float *parts, int32_t P, int64_t n, void *y, void *st
     if ((uintptr_t)parts % 16 || (uintptr_t)y % 8) return fail(WF_E_ARG, "parts must be 16-byte and y 8-byte aligned");
     const int64_t n4 = n / 4, blocks = (n4 + 255) / 256;
     wf::k_sum_ranks<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, (cudaStream_t)stream>>>(
-        (const float4 *)parts, P, n4, (uint2 *)y);
+        (const float4 *)parts, P, n4, (uint2 *)y); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "sum_ranks launch");
 }
@@ -2076,7 +2091,7 @@ int wf_moe_to_bf16(const float *src, int64_t n, void *dst, void *stream) {
     if (n <= 0 || n > (int64_t)1 << 30) return fail(WF_E_SHAPE, "n outside 1..2^30");
     const int64_t blocks = (n + 255) / 256;
     wf::k_to_bf16<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, (cudaStream_t)stream>>>(
-        src, (__nv_bfloat16 *)dst, (int)n);
+        src, (__nv_bfloat16 *)dst, (int)n); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "to_bf16 launch");
 }
@@ -2104,7 +2119,7 @@ int wf_moe_finish(const wf_moe_config *cfg, const float *yp, int32_t T, int32_t 
     const int n = T * cfg->dim;
     const __nv_bfloat16 *os =
         (const __nv_bfloat16 *)((const uint8_t *)workspace + L.os) + (size_t)row0 * cfg->dim;
-    wf::k_moe_finish<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(yp, os, (__nv_bfloat16 *)y, n);
+    wf::k_moe_finish<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(yp, os, (__nv_bfloat16 *)y, n); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "finish launch");
 }
@@ -2119,24 +2134,52 @@ int wf_moe_finish(const wf_moe_config *cfg, const float *yp, int32_t T, int32_t 
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) uint8_t g_noalloc_scratch[WF_NOALLOC_SCRATCH_BYTES];
 
-static std::mutex g_noalloc_mu;
-static void *g_noalloc_ptr[64];
+// cuCtxGetCurrent through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
 
-// Device address of g_noalloc_scratch on the current device, looked up once
-// per device.  Host code may not use the array's name as an address.
+static CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    return fn;
+}
+
+static std::mutex g_noalloc_mu;
+static std::map<std::pair<int, CUcontext>, void *> g_noalloc_ptr;
+
+// Device address of g_noalloc_scratch for the current device and context,
+// looked up once per (device, context) with that device current.  In host code
+// the array's name is only a stand-in; a kernel must get this address.
 static int noalloc_scratch(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (dev < 0 || dev >= 64) return fail(WF_E_CUDA, "device index out of range");
+    CtxGetCurrentFn get = ctx_get_current_fn();
+    if (!get) return fail(WF_E_CUDA, "cuCtxGetCurrent unavailable");
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS) return fail(WF_E_CUDA, "cuCtxGetCurrent failed");
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-        g_noalloc_ptr[dev] = p;
+    if (ctx) {
+        auto f = g_noalloc_ptr.find(std::make_pair(dev, ctx));
+        if (f != g_noalloc_ptr.end()) {
+            *out = f->second;
+            return WF_OK;
+        }
     }
-    *out = g_noalloc_ptr[dev];
+    // first call in this context: the lookup also makes the device's primary
+    // context current when the calling thread had none
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    if (get(&ctx) != CUDA_SUCCESS || !ctx) return fail(WF_E_CUDA, "no current CUDA context");
+    g_noalloc_ptr[std::make_pair(dev, ctx)] = p;
+    *out = p;
     return WF_OK;
 }
 
@@ -2149,44 +2192,65 @@ int wf_moe_forward_noalloc(const wf_moe_config *cfg, const wf_moe_weights *w, co
     c.max_tokens = T;  // size the scratch for this call only
     int rc = check_cfg(&c);
     if (rc) return rc;
-    const WsLayout L = ws_layout(&c);
+    const WsLayout L = ws_layout(&c, false);
     if (L.total > WF_NOALLOC_SCRATCH_BYTES)
         return fail(WF_E_SHAPE, "T too large for the static scratch of wf_moe_forward_noalloc (" +
                                     std::to_string(L.total) + " bytes needed, " +
                                     std::to_string((size_t)WF_NOALLOC_SCRATCH_BYTES) + " available)");
+    rc = check_expert_ptrs(w);
+    if (rc) return rc;
+    if (!y) return fail(WF_E_ARG, "null output");
     void *scratch = nullptr;
     rc = noalloc_scratch(&scratch);
     if (rc) return rc;
     wf::MoeArgs a;
-    rc = fill_args(&c, w, x, input_ids, T, scratch, WF_NOALLOC_SCRATCH_BYTES, a);
+    rc = fill_args(&c, w, x, input_ids, T, scratch, WF_NOALLOC_SCRATCH_BYTES, a, nullptr, false, false);
     if (rc) return rc;
-    if (!y) return fail(WF_E_ARG, "null output");
-    if (!w->w13 || !w->w13_s || !w->w2 || !w->w2_s || !w->shared_w13 || !w->shared_s13 ||
-        !w->shared_w2 || !w->shared_s2)
-        return fail(WF_E_ARG, "null expert weight pointer");
-    // the error word and the completion counters must start at zero; the rest
-    // is fully written before it is read
-    cudaError_t e = cudaMemsetAsync(scratch, 0, L.logits, (cudaStream_t)stream);
+    // The completion counters must start at zero (a call that timed out can leave
+    // them set); the rest is fully written before it is read.  The error word at
+    // the start of the array is left alone: it collects every call's flags until
+    // wf_moe_read_error_noalloc reads and clears it.
+    cudaError_t e = cudaMemsetAsync((uint8_t *)scratch + L.cnt_router, 0, L.logits - L.cnt_router,
+                                    (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch counters)");
     a.y = (__nv_bfloat16 *)y; a.y_partial = nullptr; a.partial = 0;
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
     return launch_moe(a, false, (cudaStream_t)stream);
 }
 
-int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream) {
-    if (!workspace || workspace_bytes < 16) return fail(WF_E_ARG, "null workspace");
+// Reads (synchronizing `stream`) and clears the error word of the static scratch.
+static int read_error_word(void *word, cudaStream_t st) {
     int host = 0;
-    cudaError_t e = cudaMemcpyAsync(&host, workspace, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    cudaError_t e = cudaMemcpyAsync(&host, word, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_fail(e, "read error word");
     if (host) {
         // read-and-clear: the next read reports only what later calls set
-        e = cudaMemsetAsync((void *)workspace, 0, 4, (cudaStream_t)stream);
+        e = cudaMemsetAsync(word, 0, 4, st);
         if (e != cudaSuccess) return cuda_fail(e, "clear error word");
     }
     if (host & wf::kErrTimeout) return fail(WF_E_TIMEOUT, "a device wait timed out");
     if (host & wf::kErrExpertId) return fail(WF_E_EXPERT_ID, "token or expert id out of range");
     return WF_OK;
+}
+
+int wf_moe_read_error_noalloc(void *stream) {
+    void *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    return read_error_word(scratch, (cudaStream_t)stream);
+}
+
+uint64_t wf_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int wf_set_wait_limit(int64_t cycles) {
+    g_wait_limit.store(cycles > 0 ? (long long)cycles : wf::kWaitLimitCycles, std::memory_order_relaxed);
+    return WF_OK;
+}
+
+int wf_moe_read_error(const void *workspace, size_t workspace_bytes, void *stream) {
+    if (!workspace || workspace_bytes < 16) return fail(WF_E_ARG, "null workspace");
+    return read_error_word(const_cast<void *>(workspace), (cudaStream_t)stream);
 }
 
 int wf_act_quant(const void *x, int64_t M, int64_t K, int32_t block, int32_t ue8m0, void *q,
@@ -2198,7 +2262,7 @@ int wf_act_quant(const void *x, int64_t M, int64_t K, int32_t block, int32_t ue8
     const long long warps = M * (K / block);
     const long long blocks = (warps * 32 + 255) / 256;
     wf::k_act_quant<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16 *)x, M, K, block, ue8m0, (uint8_t *)q, s, scale_kind == WF_SCALE_F32);
+        (const __nv_bfloat16 *)x, M, K, block, ue8m0, (uint8_t *)q, s, scale_kind == WF_SCALE_F32); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "act_quant launch");
 }
@@ -2208,7 +2272,7 @@ int wf_fp4_act_quant(const void *x, int64_t M, int64_t K, void *q, void *s, void
     if (M <= 0 || K <= 0 || K % 32) return fail(WF_E_SHAPE, "K must be a multiple of 32");
     const long long n = M * (K / 32);
     wf::k_fp4_act_quant<<<(unsigned)((n + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16 *)x, M, K, (uint8_t *)q, (uint8_t *)s);
+        (const __nv_bfloat16 *)x, M, K, (uint8_t *)q, (uint8_t *)s); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "fp4_act_quant launch");
 }
@@ -2355,6 +2419,7 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
         lc.attrs = attr;
         lc.numAttrs = 1;
         cudaError_t e = cudaLaunchKernelEx(&lc, wf::tc::k_dense_tc, t);
+        if (e == cudaSuccess) counted();
         if (e == cudaSuccess) e = cudaGetLastError();
         return e == cudaSuccess ? WF_OK : cuda_fail(e, "tc gemm launch");
     }
@@ -2376,7 +2441,7 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
     }
     const int G_ = sm_count();
     if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
-    wf::k_dense<<<G_, wf::NTHR, wf::SMEM_BYTES, st>>>(d);
+    wf::k_dense<<<G_, wf::NTHR, wf::SMEM_BYTES, st>>>(d); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "gemm launch");
 }
@@ -2412,7 +2477,7 @@ int wf_fp4_scales_in_range(const uint8_t *scales, int64_t n, void *stream) {
     int host = 0;
     e = cudaMemsetAsync(dbad, 0, 4, (cudaStream_t)stream);
     if (e == cudaSuccess && n > 0) {
-        wf::k_scale_range<<<296, 256, 0, (cudaStream_t)stream>>>(scales, n, dbad);
+        wf::k_scale_range<<<296, 256, 0, (cudaStream_t)stream>>>(scales, n, dbad); counted();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaMemcpyAsync(&host, dbad, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream);

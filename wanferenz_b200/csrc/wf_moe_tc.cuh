@@ -157,9 +157,11 @@ __device__ __forceinline__ int cta_of(long long x, long long S, int G) {
 }
 __device__ __forceinline__ long long cta_start(int b, long long S, int G) { return S * b / G; }
 
-__device__ __forceinline__ bool twait(uint64_t *bar, uint32_t parity, int *err, volatile int *abort) {
+// Wait on another role's progress (bounded by the launch's limit); a timeout stops every role.
+__device__ __forceinline__ bool twait(uint64_t *bar, uint32_t parity, int *err, volatile int *abort,
+                                      long long limit) {
     if (*abort) return false;
-    if (!wf_wait(bar, parity, err)) { *abort = 1; return false; }
+    if (!wf_wait(bar, parity, err, limit)) { *abort = 1; return false; }
     return true;
 }
 
@@ -281,7 +283,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 const TItem it = decode<PH>(a, r, cur, sg.i);
                 const uint32_t tx = it.shared ? STAGE_BYTES : STAGE_BYTES / 2;
                 for (int j = sg.j0; j < sg.j1; ++j, ++gs, lap += (st + 1 == nstg), st = (st + 1 == nstg) ? 0 : st + 1) {
-                    if (gs >= nstg && !twait(B.empty + st, (lap - 1) & 1, a.err, abort)) break;
+                    if (gs >= nstg && !twait(B.empty + st, (lap - 1) & 1, a.err, abort, a.wait_limit)) break;
                     uint8_t *dst = base + OFF_A + st * STAGE_BYTES;
                     mbar_arrive_expect_tx(B.full + st, tx);
                     if (PH == 2) {
@@ -314,11 +316,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 const TItem it = decode<PH>(a, r, cur, sg.i);
                 const int buf = sg.q & 1;
                 if (it.key != key) {
-                    if (!twait(B.b_ready, nb & 1, a.err, abort)) break;
+                    if (!twait(B.b_ready, nb & 1, a.err, abort, a.wait_limit)) break;
                     ++nb;
                     key = it.key;
                 }
-                if (sg.q >= 2 && !twait(B.d_free + buf, ((sg.q >> 1) - 1) & 1, a.err, abort)) break;
+                if (sg.q >= 2 && !twait(B.d_free + buf, ((sg.q >> 1) - 1) & 1, a.err, abort, a.wait_limit)) break;
                 tc::fence_after_sync();
                 const int afmt = it.shared ? 0 : 5;
                 const uint32_t id0 = tc::idesc_mxf8f6f4(afmt, 0, NT, 0), id1 = tc::idesc_mxf8f6f4(afmt, 0, NT, 1);
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     // weight-scale groups: K steps [8k, 8k+8) of the item, cut to the segment
                     const int gj = j & (GRP - 1);
                     if (j == sg.j0 || gj == 0) {
-                        if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort)) { ok = false; break; }
+                        if (!twait(B.sfa_ready + (gi & 1), (gi >> 1) & 1, a.err, abort, a.wait_limit)) { ok = false; break; }
                     }
                     // Every issuer waits for every stage use, not only its own: a parity
                     // wait is valid only while the barrier is at most one phase away,
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                     // otherwise see its still-pending phase as this one's.  Non-owners
                     // release the use at once; the producer refills a stage when all
                     // issuers have passed it and the owner's MMAs are done.
-                    if (!twait(B.full + st, lap & 1, a.err, abort)) { ok = false; break; }
+                    if (!twait(B.full + st, lap & 1, a.err, abort, a.wait_limit)) { ok = false; break; }
                     if (own != ii) {
                         mbar_arrive(B.empty + st);
                     } else {
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         // decision for all of them: a timeout seen by any warp stops every warp.
         bool dead = false;
         auto wwait = [&](uint64_t *bar, uint32_t parity) -> bool {
-            const bool ok = twait(bar, parity, a.err, abort);
+            const bool ok = twait(bar, parity, a.err, abort, a.wait_limit);
             if (bar_or(1, NWK, !ok)) dead = true;
             return !dead;
         };

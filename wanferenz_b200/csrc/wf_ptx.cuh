@@ -10,7 +10,11 @@
 namespace wf {
 
 // A device-side wait gives up after this many SM clock cycles (~1-2 s at
-// B200 clocks) and reports WF_ERR_TIMEOUT instead of hanging the GPU.
+// B200 clocks) and reports kErrTimeout instead of hanging the GPU.  Waits on
+// another role's progress take the limit the launch carries (this value unless
+// the host lowered it, see wf_set_wait_limit); waits for a copy or MMA this
+// thread issued itself (the drains before a CTA exits or frees TMEM) always
+// take this one, so a CTA never leaves with its own operations in flight.
 constexpr long long kWaitLimitCycles = 2000000000LL;
 
 // bits of the device error word
@@ -55,11 +59,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait for the phase with `parity` to complete.  On timeout sets
 // kErrTimeout in *err and returns false.
-__device__ __forceinline__ bool wf_wait(uint64_t *bar, uint32_t parity, int *err) {
+__device__ __forceinline__ bool wf_wait(uint64_t *bar, uint32_t parity, int *err,
+                                        long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitLimitCycles) {
+        if (clock64() - t0 > limit) {
             atomicOr(err, kErrTimeout);
             return false;
         }
