@@ -33,10 +33,10 @@ def test_unsupported_layer_declines_to_the_replaced_forward(monkeypatch):
     for step in (1, 2):
         y = b200.b200_forward(moe, x, ids)
         assert torch.equal(y, x + 1)
-        assert moe._wf_declined == {"routed experts are not FP4": step}
+        assert moe._grouped_declined == {"routed experts are not FP4": step}
     assert len(calls) == 2 and calls[0][0] is moe
     assert moe._wf_layer is False  # the bank is not rebuilt on every step
-    assert getattr(moe, "_wf_steps", 0) == 0
+    assert getattr(moe, "_grouped_steps", 0) == 0
 
 
 def test_install_without_cuda_raises_instead_of_falling_back(monkeypatch):

@@ -263,30 +263,50 @@ def stack_bank(experts, dim, inter_dim):
     return w13, w13_s, w2, w2_s
 
 
-def _layer_from_module(moe, mod, preserve=True, max_tokens=64):
-    """Builds a ``MoELayer`` from a reference ``MoE`` module (architecture.py:744-775)."""
+def _rebind_to_bank(experts, w13, w13_s, w2, w2_s, I):
+    """Expert parameters become views into the bank (``_relayout_moe(preserve=False)``,
+    fp4_grouped.py:168-186): one copy of the weights, in the bank's layout."""
+    with torch.no_grad():
+        for j, e in enumerate(experts):
+            e.w1.weight.data = w13[j, :I].view(torch.float4_e2m1fn_x2)
+            e.w3.weight.data = w13[j, I:].view(torch.float4_e2m1fn_x2)
+            e.w1.scale.data = w13_s[j, :I].view(torch.float8_e8m0fnu)
+            e.w3.scale.data = w13_s[j, I:].view(torch.float8_e8m0fnu)
+            e.w2.weight.data = w2[j].view(torch.float4_e2m1fn_x2)
+            e.w2.scale.data = w2_s[j].view(torch.float8_e8m0fnu)
+            e.w1.weight.scale = e.w1.scale
+            e.w3.weight.scale = e.w3.scale
+            e.w2.weight.scale = e.w2.scale
+
+
+def _check_supported(moe):
+    """Raises ``WfUnsupported`` unless the routed experts are FP4 and the shared expert FP8."""
+    lo, hi = moe.experts_start_idx, moe.experts_end_idx
+    experts = [moe.experts[i] for i in range(lo, hi)]
+    if not experts or experts[0].w1.weight.dtype != torch.float4_e2m1fn_x2:
+        raise WfUnsupported("routed experts are not FP4")
+    if moe.shared_experts.w1.weight.dtype != torch.float8_e4m3fn:
+        raise WfUnsupported("shared expert is not FP8")
+
+
+def bank_from_module(moe, mod, preserve=True):
+    """Host half of the load-time bank: ``(MoEWeights, MoELayer keyword arguments)`` of a
+    reference ``MoE`` module (architecture.py:744-775), on the experts' own device.
+
+    The routed experts are stacked into the ``[E_local, 2I, D/2]`` bank (fp4_grouped.py:
+    142-188) and the shared expert's w1/w3 into ``[2I, D]`` (fp8_vector.py:316-351).  With
+    ``preserve=False`` the experts' parameters are rebound as views into the bank, so
+    the weights exist once.  Raises ``WfUnsupported`` for layers the kernels do not
+    cover (routed experts not FP4, shared expert not FP8)."""
+    _check_supported(moe)
     lo, hi = moe.experts_start_idx, moe.experts_end_idx
     experts = [moe.experts[i] for i in range(lo, hi)]
     e0 = experts[0]
-    if e0.w1.weight.dtype != torch.float4_e2m1fn_x2:
-        raise WfUnsupported("routed experts are not FP4")
     sh = moe.shared_experts
-    if sh.w1.weight.dtype != torch.float8_e4m3fn:
-        raise WfUnsupported("shared expert is not FP8")
     D, I = moe.dim, e0.w1.weight.size(0)
     w13, w13_s, w2, w2_s = stack_bank(experts, D, I)
     if not preserve:
-        with torch.no_grad():
-            for j, e in enumerate(experts):
-                e.w1.weight.data = w13[j, :I].view(torch.float4_e2m1fn_x2)
-                e.w3.weight.data = w13[j, I:].view(torch.float4_e2m1fn_x2)
-                e.w1.scale.data = w13_s[j, :I].view(torch.float8_e8m0fnu)
-                e.w3.scale.data = w13_s[j, I:].view(torch.float8_e8m0fnu)
-                e.w2.weight.data = w2[j].view(torch.float4_e2m1fn_x2)
-                e.w2.scale.data = w2_s[j].view(torch.float8_e8m0fnu)
-                e.w1.weight.scale = e.w1.scale
-                e.w3.weight.scale = e.w3.scale
-                e.w2.weight.scale = e.w2.scale
+        _rebind_to_bank(experts, w13, w13_s, w2, w2_s, I)
     sw13 = torch.cat([_u8(sh.w1.weight), _u8(sh.w3.weight)])
     ss13 = torch.cat([_scale(sh.w1.scale), _scale(sh.w3.scale)])
     g = moe.gate
@@ -295,36 +315,89 @@ def _layer_from_module(moe, mod, preserve=True, max_tokens=64):
         tid2eid=getattr(g, "tid2eid", None) if g.hash else None,
         w13=w13, w13_s=w13_s, w2=w2, w2_s=w2_s, shared_w13=sw13, shared_s13=ss13,
         shared_w2=_u8(sh.w2.weight), shared_s2=_scale(sh.w2.scale))
-    ue8m0 = getattr(mod, "scale_fmt", "ue8m0") is not None
-    return MoELayer(weights, dim=D, inter_dim=I, n_experts=moe.n_routed_experts, topk=g.topk,
-                    score_func=g.score_func, route_scale=g.route_scale,
-                    swiglu_limit=e0.swiglu_limit, hash_layer=g.hash,
-                    vocab=g.tid2eid.size(0) if g.hash else 0, ue8m0=ue8m0,
-                    n_local_experts=hi - lo, expert_offset=lo, max_tokens=max_tokens)
+    kwargs = dict(dim=D, inter_dim=I, n_experts=moe.n_routed_experts, topk=g.topk,
+                  score_func=g.score_func, route_scale=float(g.route_scale),
+                  swiglu_limit=float(e0.swiglu_limit), hash_layer=bool(g.hash),
+                  vocab=g.tid2eid.size(0) if g.hash else 0,
+                  ue8m0=getattr(mod, "scale_fmt", "ue8m0") is not None,
+                  n_local_experts=hi - lo, expert_offset=lo)
+    return weights, kwargs
+
+
+def _to_device(w: MoEWeights, device):
+    return MoEWeights(**{f.name: (None if getattr(w, f.name) is None else getattr(w, f.name).to(device))
+                         for f in dataclasses.fields(w)})
+
+
+def _grouped_bank_of(layer):
+    """The layer's device bank under the reference's bank keys (fp4_grouped.py:136, 186):
+    what ``graphs/decoder.py``'s capture gate looks for as ``moe._grouped_bank``."""
+    w = layer.weights
+    return {"w13": w.w13, "w13_s": w.w13_s, "w2": w.w2, "w2_s": w.w2_s}
+
+
+def _layer_from_module(moe, mod, preserve=True, max_tokens=64):
+    """Builds a ``MoELayer`` from a reference ``MoE`` module: ``bank_from_module``, then
+    the upload to the current CUDA device (a no-op for a module already there)."""
+    weights, kwargs = bank_from_module(moe, mod, preserve=preserve)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if weights.w13.device != dev:
+        weights = _to_device(weights, dev)
+        if not preserve:
+            _rebind_to_bank([moe.experts[i] for i in range(moe.experts_start_idx, moe.experts_end_idx)],
+                            weights.w13, weights.w13_s, weights.w2, weights.w2_s, kwargs["inter_dim"])
+    return MoELayer(weights, max_tokens=max_tokens, **kwargs)
 
 
 def bank_layout(module, preserve=True, max_tokens=64):
     """Stacks every MoE in ``module`` into a load-time bank and attaches its ``MoELayer``.
 
-    Mirrors ``fp4_grouped.bank_layout`` (fp4_grouped.py:191-201); returns the
-    number of MoE modules laid out.
+    Mirrors ``fp4_grouped.bank_layout`` (fp4_grouped.py:191-201): returns the number of
+    MoE modules laid out, and leaves each one's bank in ``moe._grouped_bank`` (the
+    attribute the reference's CUDA-graph capture gate checks, graphs/decoder.py:258-264).
+    A layer the kernels do not cover is skipped, as the reference skips non-FP4 layers.
     """
     n = 0
     for m in module.modules():
         if hasattr(m, "experts") and hasattr(m, "experts_start_idx") and getattr(m, "_wf_layer", None) is None:
-            m._wf_layer = _layer_from_module(m, _MOD, preserve=preserve, max_tokens=max_tokens)
+            try:
+                m._wf_layer = _layer_from_module(m, _MOD, preserve=preserve, max_tokens=max_tokens)
+            except WfUnsupported:
+                continue
+            m._grouped_bank = _grouped_bank_of(m._wf_layer)
             n += 1
     return n
+
+
+# free device memory a lazily stacked bank must leave (fp4_grouped.py:204, _BANK_HEADROOM_BYTES)
+BANK_HEADROOM_BYTES = 2 << 30
+
+
+def _bank_fits(moe, max_tokens=64):
+    """Whether stacking this layer's bank beside its per-expert weights leaves the
+    headroom free (fp4_grouped.py:207-218): the lazy path copies the weights."""
+    lo, hi = moe.experts_start_idx, moe.experts_end_idx
+    need = sum(t.numel() * t.element_size()
+               for e in (moe.experts[i] for i in range(lo, hi))
+               for k in ("w1", "w2", "w3") for t in (getattr(e, k).weight, getattr(e, k).scale))
+    sh = moe.shared_experts
+    need += sum(t.numel() * t.element_size() for k in ("w1", "w3") for t in (getattr(sh, k).weight,
+                                                                            getattr(sh, k).scale))
+    free, _total = torch.cuda.mem_get_info()
+    return free - need >= BANK_HEADROOM_BYTES
 
 
 def _decline(self, x, input_ids, why):
     """The reference plugins' convention for a configuration they do not cover
     (fp4_grouped.py:256-262): count the reason and run the replaced forward."""
-    counts = getattr(self, "_wf_declined", None)
+    counts = getattr(self, "_grouped_declined", None)
     if counts is None:
-        counts = self._wf_declined = {}
+        counts = self._grouped_declined = {}
     counts[why] = counts.get(why, 0) + 1
     return _REF_FORWARD(self, x, input_ids)
+
+
+BANK_DECLINED = "bank does not fit beside the per-expert weights"
 
 
 def b200_forward(self, x, input_ids):
@@ -333,14 +406,21 @@ def b200_forward(self, x, input_ids):
     A configuration the kernels do not cover (``WfUnsupported``: experts not
     FP4, shared expert not FP8, shapes outside the kernels' limits, a batch over
     the workspace in the all-reduce mode) declines to the replaced forward and
-    is counted in ``self._wf_declined``; a missing CUDA device or library and
-    CUDA errors raise.  Successful steps count in ``self._wf_steps``.
+    is counted in ``self._grouped_declined``, the reference's tally
+    (fp4_grouped.py:256-262); so does a layer without a load-time bank whose
+    lazily stacked bank would not fit in free device memory (fp4_grouped.py:
+    221-232).  A missing CUDA device or library and CUDA errors raise.
+    Successful steps count in ``self._grouped_steps``, the counter the
+    reference's graph-capture probe reads (graphs/decoder.py:223-246).
     """
     layer = getattr(self, "_wf_layer", None)
     if layer is False:
         return _decline(self, x, input_ids, self._wf_unsupported)
     if layer is None:
         try:
+            _check_supported(self)
+            if not _bank_fits(self):
+                raise WfUnsupported(BANK_DECLINED)
             self._wf_layer = layer = _layer_from_module(self, _MOD)
         except WfUnsupported as e:
             self._wf_layer, self._wf_unsupported = False, str(e)
@@ -349,7 +429,7 @@ def b200_forward(self, x, input_ids):
         y = _b200_step(self, layer, x, input_ids)
     except WfUnsupported as e:
         return _decline(self, x, input_ids, str(e))
-    self._wf_steps = getattr(self, "_wf_steps", 0) + 1
+    self._grouped_steps = getattr(self, "_grouped_steps", 0) + 1
     return y
 
 
@@ -369,7 +449,12 @@ def _b200_step(self, layer, x, input_ids):
     return y.view(shape)
 
 
+# Markers: ours, and the reference's grouped-MoE marker (fp4_grouped.py:347), which
+# its lever audit (serving/controls.py:38-68) and CUDA-graph capture gate
+# (graphs/decoder.py:213-220) read: this forward is a grouped MoE forward with a
+# load-time bank and no host sync, the contract that gate stands for.
 b200_forward._wf_b200 = True
+b200_forward._v4_grouped = True
 
 
 def install(mod):
@@ -400,6 +485,6 @@ def uninstall(mod):
 
 
 def coverage(module):
-    """Per MoE layer: number of forwards the B200 path ran (cf. fp4_grouped.coverage, 327-336)."""
-    return {getattr(m, "layer_id", i): getattr(m, "_wf_steps", 0)
+    """Per MoE layer: ``(steps on the B200 path, declined reasons)`` (fp4_grouped.coverage, 327-336)."""
+    return {getattr(m, "layer_id", i): (getattr(m, "_grouped_steps", 0), dict(getattr(m, "_grouped_declined", {})))
             for i, m in enumerate(mm for mm in module.modules() if hasattr(mm, "experts_start_idx"))}
