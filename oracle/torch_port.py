@@ -70,30 +70,30 @@ def dequant_fp8(w, w_s, block=128):
     return v * s
 
 
-def _linear(x, w_deq, ue8m0):
+def _linear(x, w_deq, ue8m0, acc=torch.float32):
     """``linear`` on a quantized weight (architecture.py:121-134): act_quant, dequantized
-    product in fp32, bf16 output."""
+    product in fp32 (``acc=torch.float64``: the exact sum, rounded to fp32), bf16 output."""
     q, s = act_quant(x, 128, ue8m0)
     a = q * s.repeat_interleave(128, -1)
-    return (a @ w_deq.T).to(torch.bfloat16).to(torch.float32)
+    return (a.to(acc) @ w_deq.to(acc).T).to(torch.float32).to(torch.bfloat16).to(torch.float32)
 
 
-def _expert(x, w1, w3, w2, weights, limit, ue8m0):
+def _expert(x, w1, w3, w2, weights, limit, ue8m0, acc=torch.float32):
     """``Expert.forward`` (architecture.py:721-741) on dequantized weights."""
-    g = _linear(x, w1, ue8m0)
-    u = _linear(x, w3, ue8m0)
+    g = _linear(x, w1, ue8m0, acc)
+    u = _linear(x, w3, ue8m0, acc)
     if limit > 0:
         u = u.clamp(-limit, limit)
         g = g.clamp(max=limit)
     h = torch.nn.functional.silu(g) * u
     if weights is not None:
         h = weights * h
-    return _linear(h.to(torch.bfloat16).to(torch.float32), w2, ue8m0)
+    return _linear(h.to(torch.bfloat16).to(torch.float32), w2, ue8m0, acc)
 
 
-def gate(x, p, input_ids=None):
+def gate(x, p, input_ids=None, acc=torch.float32):
     """``Gate.forward`` (architecture.py:696-718): (weights [T, k], indices [T, k])."""
-    logits = x @ _t(p["gate_w"]).to(torch.float32).T
+    logits = (x.to(acc) @ _t(p["gate_w"]).to(acc).T).to(torch.float32)
     sf = p["score_func"]
     if sf == "softmax":
         scores = logits.softmax(-1)
@@ -112,12 +112,15 @@ def gate(x, p, input_ids=None):
     return w * p["route_scale"], indices
 
 
-def moe_forward(x, p, input_ids=None):
+def moe_forward(x, p, input_ids=None, acc=torch.float32, routing=None):
     """``MoE.forward`` (architecture.py:777-794): float32 ``x [T, D]`` (bf16-valued) ->
     bf16-valued float32 ``[T, D]``.  Local experts in ascending id; a token listing an
-    expert twice keeps its last slot (index-put semantics)."""
+    expert twice keeps its last slot (index-put semantics).  ``acc=torch.float64``
+    makes every matrix product the exact sum rounded to fp32 (the spread between the
+    two shows where the reference's own summation order decides a rounding);
+    ``routing=(weights, indices)`` replaces the gate."""
     x = _t(x).to(torch.float32)
-    w, idx = gate(x, p, input_ids)
+    w, idx = (_t(routing[0]), _t(routing[1])) if routing is not None else gate(x, p, input_ids, acc)
     y = torch.zeros_like(x)
     ue8m0, limit = p["ue8m0"], p["swiglu_limit"]
     for e in torch.unique(idx).tolist():
@@ -129,8 +132,9 @@ def moe_forward(x, p, input_ids=None):
         sl = torch.tensor([keep[t] for t in toks.tolist()], dtype=torch.int64)
         w1, w1_s, w3, w3_s, w2, w2_s = p["experts"](e)
         out = _expert(x[toks], dequant_fp4(w1, w1_s), dequant_fp4(w3, w3_s), dequant_fp4(w2, w2_s),
-                      w[toks, sl][:, None], limit, ue8m0)
+                      w[toks, sl][:, None], limit, ue8m0, acc)
         y[toks] += out
     s1, s1_s, s3, s3_s, s2, s2_s = p["shared"]
-    y = y + _expert(x, dequant_fp8(s1, s1_s), dequant_fp8(s3, s3_s), dequant_fp8(s2, s2_s), None, limit, ue8m0)
+    y = y + _expert(x, dequant_fp8(s1, s1_s), dequant_fp8(s3, s3_s), dequant_fp8(s2, s2_s), None, limit, ue8m0,
+                    acc)
     return y.to(torch.bfloat16).to(torch.float32)

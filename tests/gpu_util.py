@@ -217,3 +217,193 @@ def assert_layer_close_envelope(y, y_exact, y_fp32, what=""):
     assert rel[~ill].max(initial=0.0) <= 1e-2, f"{what}: max rel err {rel[~ill].max():.3e} > 1e-2"
     assert (d[ill] <= 2 * spread[ill] + 1e-2 * floor[ill]).all(), f"{what}: outside the reference's spread"
     return int(ill.sum())
+
+
+# --------------------------------------------------------------------------
+# re-quantization near-ties
+#
+# The reference rounds every GEMM output (gate, up, down) and the SwiGLU output
+# h to bf16, and re-quantizes h to E4M3 per 128-block (architecture.py:728-741,
+# torch_ops.py:33-49).  A value whose fp32 sum lies within a few fp32 ulps of a
+# bf16 rounding midpoint is rounded either way by equally valid fp32 summation
+# orders; through the FP8 re-quantization of h that one rounding moves a whole
+# E4M3 step of one h element, which shifts every output of the token by up to
+# ~1 %.  A token whose output misses the element-wise bound is accepted only
+# if the exact chain, with exactly one such near-midpoint rounding taken the
+# other way, reproduces the GPU output within the same bound.
+# --------------------------------------------------------------------------
+def _elem_ok(y, ref, floor):
+    return bool((np.abs(y - ref) / np.maximum(np.abs(ref), floor) <= 1e-2).all())
+
+
+def requant_alternatives(x_row, terms, ue8m0=True, limit=0.0, window=8):
+    """Outputs of one token under the exact chain (fp64 sums rounded to fp32) and,
+    for every gate / up / h / expert-output value within ``window`` fp32 ulps of a
+    bf16 rounding midpoint, the chain with that one value rounded to its other bf16
+    neighbour.
+
+    ``terms``: the token's experts in the reference's summation order (routed in
+    ascending id, then the shared expert), each ``(w1, w3, w2 dequantized float32
+    [N, K] torch tensors, route weight or None)``.  Returns ``[(label, y_row)]``."""
+    from oracle import torch_port as P
+
+    x = torch.as_tensor(x_row, dtype=torch.float32).view(1, -1)
+
+    def bf16(v):
+        return v.to(torch.bfloat16).to(torch.float32)
+
+    def lin(a, w):  # exact sum rounded to fp32, then bf16
+        q, s = P.act_quant(a, 128, ue8m0)
+        aa = (q * s.repeat_interleave(128, -1)).to(torch.float64)
+        return (aa @ w.to(torch.float64).T).to(torch.float32)
+
+    def near(v32):
+        low = (v32.view(torch.int32) & 0xFFFF).to(torch.int64)
+        return torch.nonzero((low - 0x8000).abs() <= window).flatten().tolist()
+
+    def other(v32, i):  # the other bf16 neighbour of v32[i]
+        b = bf16(v32[:, i:i + 1])
+        lo = torch.nextafter(b.to(torch.bfloat16), torch.tensor(-float("inf"), dtype=torch.bfloat16))
+        hi = torch.nextafter(b.to(torch.bfloat16), torch.tensor(float("inf"), dtype=torch.bfloat16))
+        return (hi if b.item() <= v32[0, i].item() else lo).to(torch.float32)
+
+    def expert_out(w1, w3, w2, wt, flip=None):
+        g32, u32 = lin(x, w1), lin(x, w3)
+        g, u = bf16(g32), bf16(u32)
+        if flip and flip[0] == "g":
+            g[:, flip[1]] = other(g32, flip[1])
+        if flip and flip[0] == "u":
+            u[:, flip[1]] = other(u32, flip[1])
+        if limit > 0:
+            u = u.clamp(-limit, limit)
+            g = g.clamp(max=limit)
+        pre = torch.nn.functional.silu(g) * u
+        if wt is not None:
+            pre = wt * pre
+        h = bf16(pre)
+        if flip and flip[0] == "h":
+            h[:, flip[1]] = other(pre, flip[1])
+        o32 = lin(h, w2)
+        o = bf16(o32)
+        if flip and flip[0] == "o":
+            o[:, flip[1]] = other(o32, flip[1])
+        return o, (near(g32), near(u32), near(pre), near(o32))
+
+    base, cands = [], []
+    for k, (w1, w3, w2, wt) in enumerate(terms):
+        o, (ng, nu, nh, no) = expert_out(w1, w3, w2, wt)
+        base.append(o)
+        cands += [(k, "g", i) for i in ng] + [(k, "u", i) for i in nu] + [(k, "h", i) for i in nh]
+        cands += [(k, "o", i) for i in no]
+
+    def total(outs):
+        y = torch.zeros_like(outs[0])
+        for o in outs:
+            y = y + o
+        return bf16(y)[0].numpy()
+
+    alts = [("exact", total(base))]
+    for k, kind, i in cands:
+        outs = list(base)
+        w1, w3, w2, wt = terms[k]
+        outs[k], _ = expert_out(w1, w3, w2, wt, flip=(kind, i))
+        alts.append((f"term {k} {kind}[{i}] rounded the other way", total(outs)))
+    return alts
+
+
+def assert_layer_close_requant(y, y_ref, token_terms, what="", ue8m0=True, limit=0.0):
+    """``assert_layer_close`` with the re-quantization near-ties accounted for.
+
+    Every element must meet |y - ref| <= 1e-2 * max(|ref|, 0.01 * rms(ref)), and the
+    mean absolute error over all elements must be <= 2e-3, except that a token
+    missing the element-wise bound is accepted when the exact chain with one
+    near-midpoint rounding taken the other way (``requant_alternatives``)
+    reproduces its output within that bound.  Each token carries ~10^5 rounded
+    values, a few of them within a few ulps of a midpoint, so a few tokens in 64
+    are expected to need this; more than one in 8 (at least two) fails.  ``token_terms(t) -> (x_row, terms)`` supplies the token's
+    input row and expert weights."""
+    y = np.asarray(y, np.float32)
+    y_ref = np.asarray(y_ref, np.float32)
+    assert np.isfinite(y).all(), f"{what}: non-finite output"
+    d = np.abs(y - y_ref)
+    assert d.mean() <= 2e-3, f"{what}: MAE {d.mean():.3e} > 2e-3"
+    rms = float(np.sqrt(np.mean(y_ref.astype(np.float64) ** 2)))
+    floor = 0.01 * rms
+    bad = [t for t in range(y.shape[0]) if not _elem_ok(y[t], y_ref[t], floor)]
+    explained = []
+    for t in bad:
+        x_row, terms = token_terms(t)
+        alts = requant_alternatives(x_row, terms, ue8m0=ue8m0, limit=limit)
+        hit = next((lab for lab, ya in alts if _elem_ok(y[t], ya, floor)), None)
+        assert hit is not None, (f"{what}: token {t} misses the element-wise bound and no single "
+                                 f"near-midpoint rounding of the exact chain explains it "
+                                 f"(max rel {float((d[t] / np.maximum(np.abs(y_ref[t]), floor)).max()):.3e})")
+        explained.append((t, hit))
+    print(f"[requant near-ties] {what}: {len(explained)} of {y.shape[0]} tokens explained by one rounding: "
+          f"{explained}")
+    assert len(explained) <= max(2, y.shape[0] // 8), f"{what}: too many near-tie tokens {explained}"
+    return explained
+
+
+def layer_token_terms(dl, x_f32, weights, indices):
+    """``token_terms`` for ``assert_layer_close_requant`` from a device layer's bank:
+    token t's local experts in ascending id (a duplicated id keeps its last slot),
+    dequantized on the host, then the shared expert."""
+    from oracle import torch_port as P
+
+    w = dl.weights
+    I = dl.inter_dim
+    lo = dl.expert_offset
+    cache = {}
+
+    def routed(e):
+        if e not in cache:
+            j = e - lo
+            cache[e] = (P.dequant_fp4(w.w13[j, :I].cpu(), w.w13_s[j, :I].cpu()),
+                        P.dequant_fp4(w.w13[j, I:].cpu(), w.w13_s[j, I:].cpu()),
+                        P.dequant_fp4(w.w2[j].cpu(), w.w2_s[j].cpu()))
+        return cache[e]
+
+    s13 = w.shared_s13.cpu()
+    nb = s13.shape[0] // 2
+    shared = (P.dequant_fp8(w.shared_w13[:I].cpu(), s13[:nb]), P.dequant_fp8(w.shared_w13[I:].cpu(), s13[nb:]),
+              P.dequant_fp8(w.shared_w2.cpu(), w.shared_s2.cpu()))
+
+    def terms(t):
+        out = []
+        row = np.asarray(indices[t])
+        for e in sorted(set(int(v) for v in row)):
+            if not lo <= e < lo + dl.n_local_experts:
+                continue
+            j = int(np.nonzero(row == e)[0][-1])
+            out.append((*routed(e), torch.tensor(float(weights[t][j]))))
+        out.append((*shared, None))
+        return np.asarray(x_f32[t], np.float32), out
+
+    return terms
+
+
+def quant_layer(syn, max_tokens=64, seed=0):
+    """MoELayer whose every routed expert is N(0, 0.02) bf16 (seeded torch generator on the
+    GPU) quantized by the library's fp4_act_quant, the reference's weight recipe
+    (fp4_grouped.py:368-408) at full size; gate and shared expert from the fixture."""
+    from wanferenz_b200 import ops
+
+    s = syn.spec
+    D, I, E = s.D, s.I, s.E
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w13 = torch.empty(E, 2 * I, D // 2, dtype=torch.uint8, device="cuda")
+    w13_s = torch.empty(E, 2 * I, D // 32, dtype=torch.uint8, device="cuda")
+    w2 = torch.empty(E, D, I // 2, dtype=torch.uint8, device="cuda")
+    w2_s = torch.empty(E, D, I // 32, dtype=torch.uint8, device="cuda")
+    for e in range(E):
+        q, sc = ops.fp4_act_quant((torch.randn(2 * I, D, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+        w13[e].copy_(q.view(torch.uint8))
+        w13_s[e].copy_(sc.view(torch.uint8))
+        q, sc = ops.fp4_act_quant((torch.randn(D, I, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+        w2[e].copy_(q.view(torch.uint8))
+        w2_s[e].copy_(sc.view(torch.uint8))
+    layer = device_layer(syn, [], max_tokens=max_tokens)
+    for name, t in (("w13", w13), ("w13_s", w13_s), ("w2", w2), ("w2_s", w2_s)):
+        getattr(layer.weights, name).copy_(t)
+    return layer

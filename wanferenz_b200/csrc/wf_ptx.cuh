@@ -57,10 +57,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of the phase with `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with `parity` to complete.  On timeout sets
-// kErrTimeout in *err and returns false.
+// kErrTimeout in *err and returns false.  With the default bound the thread
+// blocks in try_wait between checks of the clock; a lowered bound is kept to
+// the cycle by polling without blocking (try_wait may suspend the thread for
+// longer than a short bound).
 __device__ __forceinline__ bool wf_wait(uint64_t *bar, uint32_t parity, int *err,
                                         long long limit = kWaitLimitCycles) {
+    if (limit < kWaitLimitCycles) {
+        const long long t0 = clock64();
+        while (!mbar_test_wait(bar, parity)) {
+            if (clock64() - t0 > limit) {
+                atomicOr(err, kErrTimeout);
+                return false;
+            }
+        }
+        return true;
+    }
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
