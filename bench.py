@@ -240,7 +240,14 @@ def tc_engine():
     return os.environ.get("WF_DISABLE_TC", "0") in ("", "0")
 
 
+def fused_engine():
+    """On tcgen05 the whole layer is one launch unless WF_FUSED=0."""
+    return tc_engine() and os.environ.get("WF_FUSED", "1") != "0"
+
+
 def kernel_names():
+    if fused_engine():
+        return ["k_moe_fused"]
     if tc_engine():
         return ["k_moe_up", "k_moe_tc<2>", "k_moe_tc<3>"]
     return ["k_moe_up", "k_moe_mid", "k_moe_down"]
@@ -268,6 +275,11 @@ def step_bytes(indices, T, e0, El, router=True, shared=True):
     s2 = (D * I + (D // 128) * (I // 128)) if shared else 0
     Ts = T if shared else 0
     rb = ROUTER_BYTES if router else T * idx.shape[1] * 12
+    if fused_engine():
+        # router + token quantization + routed and shared w1/w3 + w2 + combine, one launch
+        k = (rb + T * D * 2 + T * D + T * D // 128 + n_exp * (w13 + w2) + s13 + s2 + 2 * (pairs * I + Ts * I)
+             + (pairs + Ts) * D * 2 * 2 + T * D * (2 if shared else 4))
+        return {"k_moe_fused": k, "experts": n_exp, "pairs": pairs}
     n1, n2, n3 = kernel_names()
     if tc_engine():
         # router + token quantization | routed + shared w1/w3 -> E4M3 hidden | w2 + combine

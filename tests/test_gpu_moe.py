@@ -47,10 +47,12 @@ def _layer(spec, touched, **kw):
     return _LAYERS[key]
 
 
-@pytest.fixture(params=["tcgen05", "mma_sync"])
+@pytest.fixture(params=["fused", "tcgen05", "mma_sync"])
 def engine(request, monkeypatch):
-    """Both expert engines: tcgen05 (default where scales are e8m0) and the mma.sync one."""
-    monkeypatch.setenv("WF_DISABLE_TC", "0" if request.param == "tcgen05" else "1")
+    """Every layer engine: the single-launch tcgen05 layer (default where scales are
+    e8m0), the three-launch tcgen05 one (WF_FUSED=0) and the mma.sync one."""
+    monkeypatch.setenv("WF_DISABLE_TC", "1" if request.param == "mma_sync" else "0")
+    monkeypatch.setenv("WF_FUSED", "0" if request.param == "tcgen05" else "1")
     return request.param
 
 

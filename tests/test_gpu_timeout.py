@@ -22,9 +22,10 @@ pytestmark = pytest.mark.gpu
 SPEC = F.LayerSpec(D=512, I=256, E=16, topk=4, score_func="sigmoid", route_scale=1.5, seed=71)
 
 
-@pytest.fixture(params=["tcgen05", "mma_sync"])
+@pytest.fixture(params=["fused", "tcgen05", "mma_sync"])
 def engine(request, monkeypatch):
-    monkeypatch.setenv("WF_DISABLE_TC", "0" if request.param == "tcgen05" else "1")
+    monkeypatch.setenv("WF_DISABLE_TC", "1" if request.param == "mma_sync" else "0")
+    monkeypatch.setenv("WF_FUSED", "0" if request.param == "tcgen05" else "1")
     return request.param
 
 

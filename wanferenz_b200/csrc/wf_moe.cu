@@ -1450,6 +1450,7 @@ __global__ void k_to_bf16(const float *src, __nv_bfloat16 *dst, int n) {
 }
 
 #include "wf_moe_tc.cuh"
+#include "wf_moe_fused.cuh"
 
 __global__ void __launch_bounds__(NTHR, 1) k_dense(const __grid_constant__ DenseArgs d) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1635,6 +1636,9 @@ int ensure_attrs() {
     cudaError_t e = cudaFuncSetAttribute((const void *)wf::tc::k_dense_tc,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, wf::tc::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc)");
+    e = cudaFuncSetAttribute((const void *)wf::fus::k_moe_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             wf::fus::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fused)");
     d.attr_done = true;
     return WF_OK;
 }
@@ -1728,6 +1732,13 @@ bool tc_disabled() {
     return v && v[0] && v[0] != '0';
 }
 
+// WF_FUSED=0 runs the tcgen05 expert phases as three launches (router, w1/w3,
+// w2) instead of the single fused launch.
+bool fused_disabled() {
+    const char *v = getenv("WF_FUSED");
+    return v && v[0] == '0';
+}
+
 // smem row stride: row bytes rounded up to 128, plus 16 (FP4: a warp reads one
 // 4-byte word from each of 8 rows x 4 lanes) or 32 (FP8: 8 bytes from 8 rows x
 // 4 lanes, two half-warp phases), so every access pattern is bank-conflict free
@@ -1747,14 +1758,21 @@ struct WsLayout {
         tok_pairs, ridx, rw, h, hs, o, os, cnt_router, cnt_rb, err, total;
     // tcgen05 expert phases: counters (zeroed region) and buffers after `total`
     size_t cnt_tc, xq, xs, hq, hqs, sq, sqs, part, total_tc;
+    // the fused single-launch layer (wf_moe_fused.cuh): grid-barrier counter,
+    // h-ready counters, per-class arrival counters, per-class partial slots
+    size_t fgbar, fhcnt, fcnt, fpart, total_fused;
 };
+
+// Upper bound of the 16-token groups of one forward (shared + routed).
+size_t tc_max_groups(const wf_moe_config *c) {
+    const size_t T = c->max_tokens, K = c->topk, El = c->n_local_experts;
+    return (T + 15) / 16 + std::min(El, T * K) + (T * K + 15) / 16;
+}
 
 // Upper bound of the items of one tcgen05 expert phase.
 size_t tc_max_items(const wf_moe_config *c) {
-    const size_t T = c->max_tokens, K = c->topk, El = c->n_local_experts;
     const size_t nblk = std::max((size_t)c->inter_dim / 128, (size_t)c->dim / 256);
-    const size_t groups = (T + 15) / 16 + std::min(El, T * K) + (T * K + 15) / 16;
-    return groups * std::max<size_t>(nblk, 1);
+    return tc_max_groups(c) * std::max<size_t>(nblk, 1);
 }
 
 // tc_counters = false: the layout of the allocation-free forward, which never runs
@@ -1798,6 +1816,11 @@ WsLayout ws_layout(const wf_moe_config *c, bool tc_counters = true) {
     L.sqs = take(T * I / 128);
     L.part = take((size_t)TC_MAX_GRID * 2 * (2 * 128 * wf::mtc::NT) * 4);
     L.total_tc = off;
+    L.fgbar = take(16);
+    L.fhcnt = take(tc_max_groups(c) * 4);
+    L.fcnt = take(4 * tc_max_items(c) * 4);
+    L.fpart = take((size_t)TC_MAX_GRID * 8 * (2 * 128 * wf::mtc::NT) * 4);
+    L.total_fused = off;
     return L;
 }
 
@@ -1848,8 +1871,9 @@ wf::Geo make_geo(int D, int I) {
 // Expert phases on tcgen05: needs power-of-two (e8m0) activation and shared
 // scales, 256-row output blocks, the tcgen05 workspace, aligned weight banks.
 int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, uint8_t *b,
-            size_t ws_bytes, wf::MoeArgs &a, wf::mtc::TcArgs *t) {
+            size_t ws_bytes, wf::MoeArgs &a, wf::mtc::TcArgs *t, wf::fus::FArgs *f = nullptr) {
     a.tc = 0;
+    if (f) f->gbar = nullptr;
     if (!t || tc_disabled()) return WF_OK;
     const int D = c->dim, I = c->inter_dim, El = c->n_local_experts;
     if (!c->ue8m0 || w->shared_scale_kind == WF_SCALE_F32 || D % 256 || ws_bytes < L.total_tc) return WF_OK;
@@ -1888,6 +1912,13 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
     t->sq = b + L.sq; t->sqs = b + L.sqs;
     t->part = (float *)(b + L.part);
     t->cnt = (unsigned *)(b + L.cnt_tc);
+    if (f && !fused_disabled() && ws_bytes >= L.total_fused) {
+        f->gbar = (unsigned long long *)(b + L.fgbar);
+        f->hcnt = (unsigned *)(b + L.fhcnt);
+        f->cnt = (unsigned *)(b + L.fcnt);
+        f->part = (float *)(b + L.fpart);
+        f->max_items = (int)tc_max_items(c);
+    }
     // items of 128 h-rows (w1/w3) and 256 output rows (w2) in the dispatch tables
     a.g.nh13 = 128;
     a.g.r2 = 256;
@@ -1896,7 +1927,8 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
 
 int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
               const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a,
-              wf::mtc::TcArgs *t = nullptr, bool routing_given = false, bool tc_counters = true) {
+              wf::mtc::TcArgs *t = nullptr, bool routing_given = false, bool tc_counters = true,
+              wf::fus::FArgs *f = nullptr) {
     int rc = check_cfg(c);
     if (rc) return rc;
     if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
@@ -1939,7 +1971,7 @@ int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
     a.cnt_rb = (unsigned *)(b + L.cnt_rb);
     a.err = (int *)(b + L.err);
     a.g = make_geo(a.D, a.I);
-    return fill_tc(c, w, L, b, ws_bytes, a, t);
+    return fill_tc(c, w, L, b, ws_bytes, a, t, f);
 }
 
 }  // namespace
@@ -1952,11 +1984,12 @@ int wf_device_sm_count(void) { return sm_count(); }
 
 size_t wf_moe_workspace_bytes(const wf_moe_config *cfg) {
     if (check_cfg(cfg)) return 0;
-    return ws_layout(cfg).total_tc;
+    return ws_layout(cfg).total_fused;
 }
 
 static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
-                      void *const *ev = nullptr, const wf::mtc::TcArgs *t = nullptr) {
+                      void *const *ev = nullptr, const wf::mtc::TcArgs *t = nullptr,
+                      const wf::fus::FArgs *f = nullptr) {
     int rc = ensure_attrs();
     if (rc) return rc;
     int G = sm_count();
@@ -1987,6 +2020,21 @@ static int launch_moe(wf::MoeArgs &a, bool route_only, cudaStream_t st,
         if (ev && e == cudaSuccess)
             e = cudaEventRecordWithFlags((cudaEvent_t)ev[i], st, cudaEventRecordDefault);
     };
+    if (!route_only && a.tc && f && f->gbar) {
+        // the whole layer in one launch; the timing events bracket it (0 -> 1),
+        // and events 2 and 3 mark the same end point
+        cudaLaunchConfig_t lf = lt;
+        lf.dynamicSmemBytes = wf::fus::SMEM;
+        rec(0);
+        if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lf, wf::fus::k_moe_fused, a, *t, *f)) == cudaSuccess)
+            counted();
+        rec(1);
+        rec(2);
+        rec(3);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "fused MoE kernel launch");
+        return WF_OK;
+    }
     rec(0);
     if (e == cudaSuccess && (e = cudaLaunchKernelEx(&lc, wf::k_moe_up, a)) == cudaSuccess) counted();
     rec(1);
@@ -2024,13 +2072,14 @@ int wf_moe_forward(const wf_moe_config *cfg, const wf_moe_weights *w, const void
     if (rc) return rc;
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
-    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
+    wf::fus::FArgs f;
+    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t, false, true, &f);
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
     a.sh_add = !a.partial;  // a partial forward leaves the shared rows to wf_moe_finish
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
-    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
+    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t, &f);
 }
 
 int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
@@ -2044,13 +2093,14 @@ int wf_moe_forward_timed(const wf_moe_config *cfg, const wf_moe_weights *w, cons
     if (rc) return rc;
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
-    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t);
+    wf::fus::FArgs f;
+    rc = fill_args(cfg, w, x, input_ids, T, workspace, workspace_bytes, a, &t, false, true, &f);
     if (rc) return rc;
     if (!y && !y_partial) return fail(WF_E_ARG, "need y or y_partial");
     a.y = (__nv_bfloat16 *)y; a.y_partial = y_partial; a.partial = y_partial != nullptr;
     a.sh_add = !a.partial;  // a partial forward leaves the shared rows to wf_moe_finish
     a.out_w = out_weights; a.out_idx = (long long *)out_indices;
-    return launch_moe(a, false, (cudaStream_t)stream, events, &t);
+    return launch_moe(a, false, (cudaStream_t)stream, events, &t, &f);
 }
 
 int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x, int32_t T,
@@ -2064,14 +2114,15 @@ int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const v
         return fail(WF_E_SHAPE, "shared rows outside 0..T");
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
-    rc = fill_args(cfg, w, x, nullptr, T, workspace, workspace_bytes, a, &t, true);
+    wf::fus::FArgs f;
+    rc = fill_args(cfg, w, x, nullptr, T, workspace, workspace_bytes, a, &t, true, true, &f);
     if (rc) return rc;
     a.given = 1;
     a.in_w = in_weights; a.in_idx = (const long long *)in_indices;
     a.sh0 = shared_row0; a.shT = shared_rows; a.sh_add = 1;
     a.y = nullptr; a.y_partial = y_partial; a.partial = 1;
     a.out_w = nullptr; a.out_idx = nullptr;
-    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t);
+    return launch_moe(a, false, (cudaStream_t)stream, nullptr, &t, &f);
 }
 
 int wf_moe_sum_ranks(const float *parts, int32_t P, int64_t n, void *y, void *stream) {
