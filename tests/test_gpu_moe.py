@@ -163,6 +163,55 @@ def test_prefill_256_tokens_against_torch_port(spec, engine):
     U.assert_layer_close_requant(U.to_f32(y)[keep], y_ref[keep], terms, f"T=256 {engine}")
 
 
+def test_checkpoint_loader_layer_matches_fixture_layer(tmp_path):
+    """A layer loaded by wanferenz_b200.checkpoint from a converted checkpoint (the
+    reference's tensor names and dtypes, conversion.py:55-82) gives bit-identical
+    outputs to the same weights uploaded directly."""
+    import dataclasses
+    import json
+
+    import safetensors.torch as ST
+
+    from wanferenz_b200 import checkpoint
+
+    spec = F.LayerSpec(D=512, I=256, E=16, topk=6, score_func="sqrtsoftplus", route_scale=1.5,
+                       swiglu_limit=10.0, hash_layer=True, vocab=64, seed=91)
+    syn = _syn(spec)
+    L_ID = 0  # a hash layer (layer_id < n_hash_layers)
+    dl = U.device_layer(syn, list(range(spec.E)))
+    w = dl.weights
+    I = spec.I
+    pre = f"layers.{L_ID}.ffn."
+    st = {pre + "gate.weight": w.gate_w.cpu(), pre + "gate.tid2eid": w.tid2eid.cpu()}
+    for e in range(spec.E):
+        for name, t, dt in (("w1.weight", w.w13[e, :I], torch.float4_e2m1fn_x2),
+                            ("w3.weight", w.w13[e, I:], torch.float4_e2m1fn_x2),
+                            ("w2.weight", w.w2[e], torch.float4_e2m1fn_x2),
+                            ("w1.scale", w.w13_s[e, :I], torch.float8_e8m0fnu),
+                            ("w3.scale", w.w13_s[e, I:], torch.float8_e8m0fnu),
+                            ("w2.scale", w.w2_s[e], torch.float8_e8m0fnu)):
+            st[f"{pre}experts.{e}.{name}"] = t.cpu().contiguous().view(dt)
+    for name, t, dt in (("w1.weight", w.shared_w13[:I], torch.float8_e4m3fn),
+                        ("w3.weight", w.shared_w13[I:], torch.float8_e4m3fn),
+                        ("w2.weight", w.shared_w2, torch.float8_e4m3fn),
+                        ("w1.scale", w.shared_s13[:I // 128], torch.float8_e8m0fnu),
+                        ("w3.scale", w.shared_s13[I // 128:], torch.float8_e8m0fnu),
+                        ("w2.scale", w.shared_s2, torch.float8_e8m0fnu)):
+        st[f"{pre}shared_experts.{name}"] = t.cpu().contiguous().view(dt)
+    ST.save_file(st, str(tmp_path / "model00000-mp1.safetensors"))
+    cfg = dict(dim=spec.D, moe_inter_dim=I, n_routed_experts=spec.E, n_activated_experts=spec.topk,
+               n_hash_layers=1, score_func=spec.score_func, route_scale=spec.route_scale,
+               swiglu_limit=spec.swiglu_limit, vocab_size=spec.vocab, scale_fmt="ue8m0")
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    cl = checkpoint.load_layer(str(tmp_path), L_ID, max_tokens=64)
+    x16, ids = syn.activations(9, draw=4)
+    x = U.bf16_tensor(x16)
+    tid = torch.from_numpy(ids).cuda()
+    assert torch.equal(cl.forward(x, tid), dl.forward(x, tid))
+    torch.cuda.synchronize()
+    cl.read_error()
+
+
 def test_hash_duplicates_keep_one_contribution():
     """tid2eid rows like [3,3,7,3,12,7]: each expert contributes once (fp4_grouped.py:265-268)."""
     spec = F.LayerSpec(D=256, I=128, E=16, topk=6, score_func="sqrtsoftplus", hash_layer=True,

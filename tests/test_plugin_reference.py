@@ -13,6 +13,9 @@ half of the plugin on them:
   the same output through them), and the configuration fields read from the
   module (top-k, score function, route scale, SwiGLU limit, hash routing and its
   vocabulary, the expert shard of rank 1 of 2);
+* ``checkpoint.read_layer``: a converted checkpoint holding the module (its
+  state_dict under ``layers.{L}.ffn.``, ``config.json`` from ``ModelArgs``) reads
+  into the same bank bytes and configuration as the module relayout;
 * the reference's CUDA-graph capture gate (graphs/decoder.py:249-272) and lever
   audit (serving/controls.py:38-68) on a module with the plugin installed: the
   chain starts with the grouped marker, the bank is found, and the probe step
@@ -106,10 +109,32 @@ def _child(ref_dir, q):
             "rank1of2": (F.LayerSpec(D=256, I=128, E=16, topk=4, score_func="softmax", route_scale=1.0,
                                      seed=83), 3, 1, 1),
         }
+        import dataclasses
+        import json
+        import tempfile
+
+        import safetensors.torch as ST
+
+        from wanferenz_b200 import checkpoint
+
         for name, (spec, T, layer_id, rank) in specs.items():
             mod.world_size, mod.rank = (2, rank) if name == "rank1of2" else (1, 0)
             moe, layer = _build_moe(mod, torch, spec, layer_id)
             lo, hi = moe.experts_start_idx, moe.experts_end_idx
+            # a converted checkpoint holding this layer, under the names a stage's
+            # load reads (layers.{L}.ffn.*; partition.py:759-801, chain.py:2105-2117)
+            ckpt = tempfile.mkdtemp(prefix="wf_ckpt_")
+            state = {f"layers.{layer_id}.ffn.{k}": v.detach().clone().contiguous()
+                     for k, v in moe.state_dict().items()}
+            ST.save_file(state, os.path.join(ckpt, "model00000-mp1.safetensors"))
+            margs = mod.ModelArgs(dim=spec.D, moe_inter_dim=spec.I, n_routed_experts=spec.E,
+                                  n_activated_experts=spec.topk, n_shared_experts=1,
+                                  n_hash_layers=1 if spec.hash_layer else 0, score_func=spec.score_func,
+                                  route_scale=spec.route_scale, swiglu_limit=spec.swiglu_limit,
+                                  expert_dtype="fp4", vocab_size=spec.vocab)
+            with open(os.path.join(ckpt, "config.json"), "w") as fh:
+                json.dump(dataclasses.asdict(margs), fh)
+            cw, ckw = checkpoint.read_layer(ckpt, layer_id, rank=mod.rank, world=mod.world_size, device="cpu")
             before = {e: [getattr(moe.experts[e], k).weight.view(torch.uint8).clone() for k in ("w1", "w3", "w2")]
                       for e in range(lo, hi)}
             x16, ids = layer.activations(T)
@@ -137,6 +162,15 @@ def _child(ref_dir, q):
                 same &= bool(torch.equal(w.w13[j, :I], before[e][0]) and torch.equal(w.w13[j, I:], before[e][1])
                              and torch.equal(w.w2[j], before[e][2]))
             r["views"], r["bytes_kept"] = bool(views), bool(same)
+            fields = ("gate_w", "gate_b", "tid2eid", "w13", "w13_s", "w2", "w2_s", "shared_w13", "shared_s13",
+                      "shared_w2", "shared_s2")
+            r["checkpoint_bank_equal"] = all(
+                (getattr(cw, f) is None and getattr(w, f) is None) or
+                (getattr(cw, f) is not None and getattr(w, f) is not None and
+                 torch.equal(getattr(cw, f).view(torch.uint8) if getattr(cw, f).dtype != torch.float32 else getattr(cw, f),
+                             getattr(w, f).view(torch.uint8) if getattr(w, f).dtype != torch.float32 else getattr(w, f)))
+                for f in fields)
+            r["checkpoint_kwargs_equal"] = ckw == kw
             if mod.world_size == 1:
                 with torch.no_grad():
                     y1 = mod.MoE.forward(moe, x, tid)
@@ -198,6 +232,15 @@ def test_bank_from_reference_module(results):
         assert r["bytes_kept"], f"{name}: the bank does not hold the experts' bytes"
         if name != "rank1of2":
             assert r["forward_unchanged"], f"{name}: the reference forward changed after the relayout"
+
+
+def test_checkpoint_loader_matches_module_bank(results):
+    """wanferenz_b200.checkpoint reads a converted checkpoint of the reference's module
+    (its state_dict under layers.{L}.ffn., config.json from ModelArgs) straight into
+    the same bank bytes and configuration as the module relayout."""
+    for name in ("sigmoid", "hash", "rank1of2"):
+        assert results[name]["checkpoint_bank_equal"], name
+        assert results[name]["checkpoint_kwargs_equal"], name
 
 
 def test_config_fields_read_from_reference_module(results):
