@@ -71,8 +71,11 @@ def parse():
                     help="skip the config-3 and config-4 sub-results of the default line")
     ap.add_argument("--suite", default="moe", choices=("moe", "fp8_gemm"),
                     help="fp8_gemm: BASELINE config 3, the FP8 block-scaled GEMM sweep (one JSON line, N=1)")
+    ap.add_argument("--ep", default="p2p", choices=("p2p", "nccl"),
+                    help="N > 1: p2p = tokens, routing and partial rows moved over NVLink by the fused kernel "
+                         "(wf_moe_forward_ep_p2p); nccl = route, NCCL all-gather, expert forward, NCCL combine")
     ap.add_argument("--combine", default="reduce_scatter", choices=("reduce_scatter", "all_to_all"),
-                    help="N > 1: NCCL reduce-scatter of the partials, or all-to-all + ascending-rank sum")
+                    help="--ep nccl: NCCL reduce-scatter of the partials, or all-to-all + ascending-rank sum")
     ap.add_argument("--init", default="quant", choices=("quant", "random"),
                     help="quant: N(0,0.02) weights through the FP4 quantizer; random: random FP4 bytes "
                          "with typical scales (fewer launches, for profiler captures)")
@@ -296,6 +299,20 @@ def step_bytes(indices, T, e0, El, router=True, shared=True):
 EP_PHASES = ["route", "all_gather", "experts", "combine", "to_bf16"]
 
 
+def p2p_step_bytes(idx_g, Tloc, world, e0, El):
+    """Bytes of one expert-parallel step over peer memory, per rank: the router over
+    the rank's own tokens, its local experts on the gathered batch, the shared expert
+    on its own rows, the tokens / routing / partial rows it sends over NVLink and the
+    finish's reads."""
+    rt = step_bytes(idx_g, Tloc * world, e0, El, router=False, shared=False)
+    s13 = 2 * I * D + 2 * (I // 128) * (D // 128)
+    s2 = D * I + (D // 128) * (I // 128)
+    sent = (world - 1) * Tloc * (D + D // 128 + 8 * K_TOP) + (world - 1) * Tloc * D * 4
+    k = (ROUTER_BYTES + Tloc * D * 2 + sum(rt[n] for n in kernel_names()) + s13 + s2 + Tloc * (I * 2 + D * 2 * 2)
+         + sent + world * Tloc * D * 4 + Tloc * D * 2)
+    return {"ep_step": k, "experts_touched": rt["experts"], "pairs": rt["pairs"], "nvlink_bytes_sent": sent}
+
+
 def ep_step_bytes(idx_g, Tloc, world, e0, El, combine="reduce_scatter"):
     """Per-phase bytes of one expert-parallel step (``wanferenz_b200.ep.ep_forward``)."""
     import numpy as np
@@ -332,6 +349,7 @@ def run_gpu(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    dom_name = None
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
@@ -345,6 +363,7 @@ def run_gpu(args):
     zb = args.zipf_beta if args.routing == "zipf" else 0.0
     layers = [make_layer(s, rank, world, max(Tg, 16), dev, args.init, zb) for s in range(args.layers)]
     lib = L.load()
+    peers = [ep.PeerGroup(lay) for lay in layers] if world > 1 and args.ep == "p2p" else []
     hbm, peak_kind = peaks()
     torch.cuda.synchronize()
 
@@ -407,9 +426,18 @@ def run_gpu(args):
             if ev:
                 ev[5].record()
 
+        def one_p2p(i, timed=False):
+            """``wanferenz_b200.ep.PeerGroup.forward``: one call, the fused kernel and the finish."""
+            ev = pev[i] if timed else None
+            if ev:
+                ev[0].record()
+            peers[i % len(peers)].forward(xs[i], out=ys[i], out_routing=(rw[i], ri[i]))
+            if ev:
+                ev[1].record()
+
         def one(i, timed=False):
             if world > 1:
-                return one_ep(i, timed)
+                return one_p2p(i, timed) if args.ep == "p2p" else one_ep(i, timed)
             lay = lays[i % len(lays)]
             st = L.stream_ptr()
             ev = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(e.cuda_event) for e in evs[i]])
@@ -458,12 +486,16 @@ def run_gpu(args):
             one(i, timed=True)
         torch.cuda.synchronize()
         del big
-        names = kernel_names() if world == 1 else EP_PHASES
+        names = kernel_names() if world == 1 else (["ep_step"] if args.ep == "p2p" else EP_PHASES)
         kern = {k: [] for k in names}
         for i in range(W, n):
             e = evs[i] if world == 1 else pev[i]
             for j, k in enumerate(names):
                 kern[k].append(e[j].elapsed_time(e[j + 1]))
+        if world > 1 and args.ep == "p2p":
+            # this rank's routing of its own tokens; the accounting wants the gathered batch's
+            for i in range(W, n):
+                dist.all_gather_into_tensor(idx[i], ri[i])
         routing = [idx[i].cpu().numpy() for i in range(W, n)]
         del g
         return reps, kern, routing, clk.summary(), launches
@@ -479,12 +511,15 @@ def run_gpu(args):
         lay0 = lays[0]
         if world == 1:
             byts = [step_bytes(r, Tloc, lay0.expert_offset, lay0.n_local_experts) for r in routing]
+        elif args.ep == "p2p":
+            byts = [p2p_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts) for r in routing]
         else:
             byts = [ep_step_bytes(r, Tloc, world, lay0.expert_offset, lay0.n_local_experts, args.combine)
                     for r in routing]
         mean = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
         kms = {k: float(np.mean(v)) for k, v in kern.items()}
-        layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else ["route", "experts", "to_bf16"]))
+        layer_bytes = sum(mean[k] for k in (kernel_names() if world == 1 else
+                                            (["ep_step"] if args.ep == "p2p" else ["route", "experts", "to_bf16"])))
         hist = [np.bincount(r.ravel(), minlength=E) for r in routing]
         tpe = {"experts_empty": float(np.mean([(h == 0).sum() for h in hist])),
                "experts_over_16": float(np.mean([(h > 16).sum() for h in hist])),
@@ -520,6 +555,8 @@ def run_gpu(args):
     # the dominant HBM-bound kernel (multi-GPU: of the compute phases; the collectives
     # are reported in kernel_us beside them)
     dom = max((k for k in kms if k not in ("all_gather", "combine")), key=kms.get)
+    if dom == "ep_step":
+        dom_name = "k_moe_fused + k_ep_finish (expert parallelism over peer memory)"
     ach = main["bytes"][dom] / (kms[dom] * 1e-3) / 1e9
     value = T * world / (main["ms"] * 1e-3)
     traffic, traffic_src = None, None
@@ -530,7 +567,7 @@ def run_gpu(args):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(layers, T, args.steps, args.warmup, dev, world, rank, args.combine)
+        e2e = run_e2e(layers, T, args.steps, args.warmup, dev, world, rank, args.combine, peers)
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 5),
@@ -542,9 +579,11 @@ def run_gpu(args):
                               "and timed with CUDA events on the launching stream; the step time is the median "
                               "replay / K" + (" (each replay's time the max over ranks)" if world > 1 else "")),
                    "replays": args.replays, "replay_ms": [round(v, 4) for v in main["reps_ms"]]},
-        "detail": {**summary(main, T), "combine": args.combine if world > 1 else None,
+        "detail": {**summary(main, T), "ep": args.ep if world > 1 else None,
+                   "combine": args.combine if world > 1 and args.ep == "nccl" else None,
                    "sweep": sweep, **extras},
-        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
+        "roofline": {"bound": "hbm", "kernel": dom_name if dom == "ep_step" else dom, "achieved": round(ach, 1),
+                     "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / hbm, 4),
                      "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": round(main["bytes"][dom])},
@@ -555,6 +594,8 @@ def run_gpu(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(T)
+    for pg in peers:
+        pg.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -562,7 +603,7 @@ def run_gpu(args):
         print(json.dumps(out), flush=True)
 
 
-def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter"):
+def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter", peers=()):
     """Public API (MoELayer.forward), host pinned input -> device -> host output every step."""
     import torch
     import torch.distributed as dist
@@ -577,6 +618,8 @@ def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter"):
         xd.copy_(xh[i], non_blocking=True)
         if world == 1:
             y = lay.forward(xd)
+        elif peers:
+            y = peers[i % len(peers)].forward(xd)
         else:
             from wanferenz_b200.ep import ep_forward
             y = ep_forward(lay, xd, combine=combine)
@@ -601,7 +644,8 @@ def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter"):
     return {"value": round(T * world / (ms * 1e-3), 1), "unit": "tokens/s",
             "us_per_step": round(ms * 1e3, 2), "h2d_bytes_per_step": T * D * 2,
             "d2h_bytes_per_step": T * D * 2,
-            "api": "wanferenz_b200.moe.MoELayer.forward" if world == 1 else "wanferenz_b200.ep.ep_forward"}
+            "api": ("wanferenz_b200.moe.MoELayer.forward" if world == 1 else
+                    "wanferenz_b200.ep.PeerGroup.forward" if peers else "wanferenz_b200.ep.ep_forward")}
 
 
 # ---------------------------------------------------------------------------

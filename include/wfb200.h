@@ -6,7 +6,8 @@
  * the kernels leave their counters at zero after every call.
  * Every entry point returns an int status (WF_OK or a negative WF_E_* code);
  * wf_last_error() returns the message of the last failure on the calling
- * host thread.  No entry point allocates device memory, synchronizes the
+ * host thread.  No entry point allocates device memory (except the set-up
+ * call wf_ep_alloc, which says so), synchronizes the
  * stream or reads device data back, except the load-time check
  * wf_fp4_scales_in_range() and the error-word reads wf_moe_read_error() and
  * wf_moe_read_error_noalloc(), which say so.
@@ -176,6 +177,50 @@ int wf_moe_forward_ep(const wf_moe_config *cfg, const wf_moe_weights *w, const v
                       const float *in_weights, const int64_t *in_indices, int32_t shared_row0,
                       int32_t shared_rows, float *y_partial, void *workspace, size_t workspace_bytes,
                       void *stream);
+
+/* ---- expert parallelism over peer memory ------------------------------
+ * The reference's expert parallelism (MoE.forward under world_size > 1,
+ * architecture.py:749-756, 785-794) routes the whole batch on every rank and
+ * all-reduces the fp32 partial sums.  Here each rank routes only its own
+ * tokens, and one fused launch moves the data over NVLink itself: the rank's
+ * E4M3-quantized tokens and their routing go straight into every rank's
+ * buffer, each rank runs its local experts on the gathered batch (and the
+ * shared expert on its own rows), and writes each token's fp32 partial row
+ * into the owner's buffer; a finish kernel sums the ranks' rows in rank
+ * order and casts to bf16.  Ranks hand off through epoch flags in the
+ * buffers (each rank's buffer counts its completed forwards, so captured CUDA
+ * graphs replay correctly); every wait is bounded (WF_E_TIMEOUT).  Set-up: every rank
+ * allocates one buffer (wf_ep_alloc, wf_ep_buffer_bytes), exports it
+ * (wf_ipc_get_handle), and opens every other rank's (wf_ipc_open_handle). */
+#define WF_IPC_HANDLE_BYTES 64
+#define WF_EP_MAX_RANKS 8
+
+/* Bytes of the per-rank buffer for `world` ranks; cfg->max_tokens is the
+ * capacity of the gathered batch (world x tokens per rank). */
+size_t wf_ep_buffer_bytes(const wf_moe_config *cfg, int32_t world);
+
+/* Set-up only (the one entry point that allocates): cudaMalloc of an
+ * expert-parallel buffer, zero-filled; wf_ep_free releases it. */
+int wf_ep_alloc(size_t bytes, void **buf);
+int wf_ep_free(void *buf);
+
+/* CUDA IPC of a buffer between the ranks' processes: export (64 bytes),
+ * map another process's buffer into this one, unmap. */
+int wf_ipc_get_handle(const void *buf, void *handle);
+int wf_ipc_open_handle(const void *handle, void **buf);
+int wf_ipc_close_handle(void *buf);
+
+/* One expert-parallel layer forward of this rank's T tokens x [T, D] (bf16),
+ * on the fused engine: bufs[p] is rank p's buffer as mapped in this process
+ * (bufs[rank] this rank's own); every rank of the group makes the same
+ * sequence of calls, one stream each.  cfg: the rank's shard
+ * (n_local_experts = E / world, expert_offset = rank * n_local_experts) and
+ * max_tokens >= world * T.  Writes y [T, D] bf16 and, optionally, this rank's
+ * routing (out_weights / out_indices [T, topk]).  Launches 2 kernels. */
+int wf_moe_forward_ep_p2p(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                          const int64_t *input_ids, int32_t T, int32_t rank, int32_t world,
+                          void *const *bufs, void *y, float *out_weights, int64_t *out_indices,
+                          void *workspace, size_t workspace_bytes, void *stream);
 
 /* dst[i] = bf16(src[i]) for i < n (round to nearest even): the last step of
  * MoE.forward's output (architecture.py:794) after the cross-rank sum. */

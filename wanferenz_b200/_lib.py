@@ -25,7 +25,8 @@ EXPORTS = (
     "wf_fp8_gemm", "wf_fp4_gemm", "wf_grouped_fp4_gemm", "wf_gemm_workspace_bytes",
     "wf_fp4_scales_in_range", "wf_moe_forward_noalloc", "wf_moe_forward_ep", "wf_moe_to_bf16",
     "wf_moe_sum_ranks", "wf_moe_read_error_noalloc", "wf_set_wait_limit",
-    "wf_launch_count",
+    "wf_launch_count", "wf_ep_buffer_bytes", "wf_ep_alloc", "wf_ep_free", "wf_ipc_get_handle",
+    "wf_ipc_open_handle", "wf_ipc_close_handle", "wf_moe_forward_ep_p2p",
 )
 
 
@@ -92,6 +93,15 @@ def _declare(lib):
         "wf_moe_read_error_noalloc": (ctypes.c_int, [P]),
         "wf_set_wait_limit": (ctypes.c_int, [I64]),
         "wf_launch_count": (ctypes.c_uint64, []),
+        "wf_ep_buffer_bytes": (SZ, [ctypes.POINTER(MoeConfig), I32]),
+        "wf_ep_alloc": (ctypes.c_int, [SZ, ctypes.POINTER(ctypes.c_void_p)]),
+        "wf_ep_free": (ctypes.c_int, [P]),
+        "wf_ipc_get_handle": (ctypes.c_int, [P, P]),
+        "wf_ipc_open_handle": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),
+        "wf_ipc_close_handle": (ctypes.c_int, [P]),
+        "wf_moe_forward_ep_p2p": (ctypes.c_int, [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeights), P, P,
+                                                 I32, I32, I32, ctypes.POINTER(ctypes.c_void_p),
+                                                 P, P, P, P, SZ, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

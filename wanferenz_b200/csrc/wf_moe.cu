@@ -69,6 +69,11 @@ constexpr int ROUTE_BYTES = ROUTE_TABLE_BYTES > TOPK_ROUTE_BYTES ? ROUTE_TABLE_B
 constexpr int SMEM_BYTES = OFF_ROUTE + ROUTE_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
+constexpr int EP_MAX_RANKS = 8;  // expert-parallel ranks over peer memory
+constexpr int EP_CTR = 2 * EP_MAX_RANKS;       // flag word: epoch of the last completed forward
+constexpr int EP_FIN = 2 * EP_MAX_RANKS + 1;   // flag word: finish blocks done
+constexpr int EP_FLAG_WORDS = 2 * EP_MAX_RANKS + 2;
+
 enum { EP_RSWIGLU = 1, EP_SSWIGLU = 2, EP_SOUT = 3, EP_ROUT = 4, EP_DENSE = 5 };
 enum { BS_XPAIR = 1, BS_XTOK = 2, BS_H = 3, BS_HS = 4, BS_PREQ = 5 };
 enum { FMT_FP4 = 0, FMT_FP8 = 1 };
@@ -118,6 +123,20 @@ struct MoeArgs {
     int sh0, shT, sh_add;
     // bound (SM cycles) of waits on another role's progress (wf_set_wait_limit)
     long long wait_limit;
+    // expert parallelism over peer memory (wf_moe_forward_ep_p2p, fused engine only):
+    // this rank routes its own Tr tokens, which are rows [ep_rank * Tr, +Tr) of the
+    // gathered batch of T = ep_world * Tr rows; the buffers below are every rank's
+    // (index ep_rank is this rank's own, in local memory)
+    int ep, ep_rank, ep_world, Tr;
+    uint8_t *ep_xq[EP_MAX_RANKS];     // gathered E4M3 tokens [T, D]
+    uint8_t *ep_xs[EP_MAX_RANKS];     // their e8m0 scales [T, D/128]
+    int *ep_ridx[EP_MAX_RANKS];       // gathered routing [T, topk] expert ids
+    float *ep_rw[EP_MAX_RANKS];       // and weights
+    float *ep_yrecv[EP_MAX_RANKS];    // partial rows of the owner's tokens from every rank [P][Tr][D]
+    // [0, P): dispatch epochs, [EP_MAX_RANKS, +P): combine epochs, [EP_CTR]: the
+    // epoch of the last completed forward (this rank's; read at the start)
+    unsigned *ep_flags[EP_MAX_RANKS];
+    unsigned *ep_done;                // local: 256-row output blocks combined in this launch
 };
 
 // Dense GEMM (operator entry points) arguments.
@@ -1152,7 +1171,12 @@ __device__ void combine_rows_v8(const MoeArgs &a, int row0, int nrows, const uin
                         acc[2 * e + 1] += bf16_bits_to_f32(u[e] >> 16);
                     }
                 }
-                float4 *dst = reinterpret_cast<float4 *>(a.y_partial + (size_t)t * D + r);
+                // expert parallelism over peer memory: the row goes to its owner's
+                // receive buffer, in this rank's slot
+                const int o = a.ep ? t / a.Tr : 0;
+                float *drow = a.ep ? a.ep_yrecv[o] + ((size_t)a.ep_rank * a.Tr + (t - o * a.Tr)) * D
+                                   : a.y_partial + (size_t)t * D;
+                float4 *dst = reinterpret_cast<float4 *>(drow + r);
                 dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
                 dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
             } else {
@@ -2173,6 +2197,128 @@ int wf_moe_finish(const wf_moe_config *cfg, const float *yp, int32_t T, int32_t 
     wf::k_moe_finish<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(yp, os, (__nv_bfloat16 *)y, n); counted();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WF_OK : cuda_fail(e, "finish launch");
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism over peer memory.  Every rank holds one buffer of the same
+// layout; the ranks map each other's buffers (CUDA IPC) and the fused kernel
+// writes tokens, routing and partial output rows straight into them.
+// ---------------------------------------------------------------------------
+struct EpLayout {
+    size_t flags, xq, xs, ridx, rw, yrecv, total;
+};
+
+static EpLayout ep_layout(const wf_moe_config *c, int world) {
+    EpLayout L{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    const size_t Tg = (size_t)c->max_tokens, D = c->dim, K = c->topk;
+    const size_t Tr = Tg / (size_t)std::max(world, 1);
+    L.flags = take(wf::EP_FLAG_WORDS * 4);
+    L.xq = take(Tg * D);
+    L.xs = take(Tg * D / 128);
+    L.ridx = take(Tg * K * 4);
+    L.rw = take(Tg * K * 4);
+    L.yrecv = take((size_t)world * Tr * D * 4);
+    L.total = off;
+    return L;
+}
+
+size_t wf_ep_buffer_bytes(const wf_moe_config *cfg, int32_t world) {
+    if (check_cfg(cfg)) return 0;
+    if (world < 1 || world > wf::EP_MAX_RANKS) return (size_t)fail(WF_E_SHAPE, "world outside 1..8"), 0;
+    return ep_layout(cfg, world).total;
+}
+
+int wf_ep_alloc(size_t bytes, void **buf) {
+    if (!buf || !bytes) return fail(WF_E_ARG, "null output or zero size");
+    cudaError_t e = cudaMalloc(buf, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*buf, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "expert-parallel buffer");
+}
+
+int wf_ep_free(void *buf) {
+    cudaError_t e = cudaFree(buf);
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "cudaFree(expert-parallel buffer)");
+}
+
+int wf_ipc_get_handle(const void *buf, void *handle) {
+    if (!buf || !handle) return fail(WF_E_ARG, "null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(buf));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == WF_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return WF_OK;
+}
+
+int wf_ipc_open_handle(const void *handle, void **buf) {
+    if (!buf || !handle) return fail(WF_E_ARG, "null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(buf, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int wf_ipc_close_handle(void *buf) {
+    cudaError_t e = cudaIpcCloseMemHandle(buf);
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int wf_moe_forward_ep_p2p(const wf_moe_config *cfg, const wf_moe_weights *w, const void *x,
+                          const int64_t *input_ids, int32_t T, int32_t rank, int32_t world,
+                          void *const *bufs, void *y, float *out_weights, int64_t *out_indices,
+                          void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_expert_ptrs(w);
+    if (rc) return rc;
+    if (!bufs || !y) return fail(WF_E_ARG, "null buffers or output");
+    if (world < 1 || world > wf::EP_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(WF_E_SHAPE, "rank / world outside 0..world-1 / 1..8");
+    if (T <= 0 || (int64_t)T * world > cfg->max_tokens)
+        return fail(WF_E_SHAPE, "world * T exceeds max_tokens (the gathered batch's capacity)");
+    for (int p = 0; p < world; ++p)
+        if (!bufs[p]) return fail(WF_E_ARG, "null peer buffer");
+    wf::MoeArgs a;
+    wf::mtc::TcArgs t;
+    wf::fus::FArgs f;
+    rc = fill_args(cfg, w, x, input_ids, T * world, workspace, workspace_bytes, a, &t, false, true, &f);
+    if (rc) return rc;
+    if (!a.tc || !f.gbar)
+        return fail(WF_E_ARG, "expert parallelism over peer memory needs the fused tcgen05 engine "
+                              "(e8m0 scales, the full workspace, WF_FUSED unset)");
+    const EpLayout E = ep_layout(cfg, world);
+    a.ep = 1; a.ep_rank = rank; a.ep_world = world; a.Tr = T;
+    for (int p = 0; p < world; ++p) {
+        uint8_t *b = (uint8_t *)bufs[p];
+        a.ep_xq[p] = b + E.xq; a.ep_xs[p] = b + E.xs;
+        a.ep_ridx[p] = (int *)(b + E.ridx); a.ep_rw[p] = (float *)(b + E.rw);
+        a.ep_yrecv[p] = (float *)(b + E.yrecv); a.ep_flags[p] = (unsigned *)(b + E.flags);
+    }
+    uint8_t *mine = (uint8_t *)bufs[rank];
+    a.xq = mine + E.xq;  // the gathered batch lives in this rank's buffer
+    a.xs = mine + E.xs;
+    t.xq = a.xq;
+    t.xs = a.xs;
+    a.ridx = (int *)(mine + E.ridx);
+    a.rw = (float *)(mine + E.rw);
+    a.ep_done = a.cnt_router;  // a workspace counter no other path of the fused engine uses
+    a.sh0 = rank * T; a.shT = T; a.sh_add = 1;  // the shared expert on this rank's tokens
+    a.y = nullptr; a.y_partial = nullptr; a.partial = 1;
+    a.out_w = out_weights; a.out_idx = (long long *)out_indices;
+    rc = launch_moe(a, false, (cudaStream_t)stream, nullptr, &t, &f);
+    if (rc) return rc;
+    const int64_t n = (int64_t)T * cfg->dim;
+    const int blocks = (int)std::min<int64_t>(1024, (n + 255) / 256);
+    wf::fus::k_ep_finish<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+        (unsigned *)(mine + E.flags), (const float *)(mine + E.yrecv), world, T, cfg->dim,
+        (__nv_bfloat16 *)y, a.err, a.wait_limit); counted();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WF_OK : cuda_fail(e, "expert-parallel finish launch");
 }
 
 // ---------------------------------------------------------------------------

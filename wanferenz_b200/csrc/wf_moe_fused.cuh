@@ -245,6 +245,16 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     return v;
 }
 
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Bounded spin of one thread until *p >= target; false (kErrTimeout set) when the
 // bound runs out or another CTA already reported a timeout.
 template <typename T, typename Load>
@@ -279,11 +289,76 @@ __device__ __forceinline__ bool grid_barrier(const FArgs &f, int *err, long long
 }
 
 // ---------------------------------------------------------------------------
+// expert parallelism over peer memory
+// ---------------------------------------------------------------------------
+// Every rank's CTA 0 (after the rank's own grid barrier) publishes this launch's
+// epoch in every rank's dispatch flags; each CTA then waits (bounded) until all
+// ranks' flags carry it: every rank's tokens and routing are in this rank's buffer.
+__device__ __forceinline__ bool ep_dispatch_handshake(const MoeArgs &a, unsigned epoch, volatile int *flag) {
+    bar_sync(2, NWK);
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) {
+            __threadfence_system();
+            for (int p = 0; p < a.ep_world; ++p) st_release_sys_u32(a.ep_flags[p] + a.ep_rank, epoch);
+        }
+        bool ok = true;
+        for (int p = 0; p < a.ep_world && ok; ++p)
+            ok = spin_until(a.ep_flags[a.ep_rank] + p, epoch, a.err, a.wait_limit, ld_acquire_sys_u32);
+        *flag = ok ? 1 : 0;
+    }
+    bar_sync(2, NWK);
+    return *flag != 0;
+}
+
+// After a 256-row output block's combine wrote its rows to their owners: the CTA
+// that completes the last block publishes the epoch in every rank's combine flags.
+__device__ __forceinline__ void ep_block_done(const MoeArgs &a, unsigned epoch, int nblocks, int bar_id) {
+    __threadfence_system();
+    bar_sync(bar_id, NWK);
+    if (threadIdx.x == 0) {
+        const unsigned old = atomicAdd(a.ep_done, 1u);
+        if (old == (unsigned)nblocks - 1) {
+            *a.ep_done = 0u;
+            __threadfence_system();
+            for (int p = 0; p < a.ep_world; ++p)
+                st_release_sys_u32(a.ep_flags[p] + EP_MAX_RANKS + a.ep_rank, epoch);
+        }
+    }
+}
+
+// act_quant of this rank's tokens t = b, b + G, ... (rows ep_rank * Tr + t of the
+// gathered batch), written to every rank's buffer.
+__device__ void quantize_tokens_ep(const MoeArgs &a) {
+    const int lane = threadIdx.x & 31;
+    const int nb = a.D / 128;
+    for (int t = blockIdx.x; t < a.Tr; t += gridDim.x) {
+        const size_t grow = (size_t)a.ep_rank * a.Tr + t;
+        for (int b = 0; b < nb; ++b) {
+            const uint2 u = __ldg(reinterpret_cast<const uint2 *>(a.x + (size_t)t * a.D + b * 128 + 4 * lane));
+            const float v0 = bf16_bits_to_f32(u.x & 0xffffu), v1 = bf16_bits_to_f32(u.x >> 16);
+            const float v2 = bf16_bits_to_f32(u.y & 0xffffu), v3 = bf16_bits_to_f32(u.y >> 16);
+            float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float s = round_scale_e8(fmaxf(m, 1e-4f), 1);
+            const float inv = 1.0f / s;  // exact: s is a power of two
+            auto qz = [&](float v) { return fminf(fmaxf(v * inv, -448.f), 448.f); };
+            const uint32_t q = (uint32_t)f32x2_to_e4m3x2(qz(v0), qz(v1)) | ((uint32_t)f32x2_to_e4m3x2(qz(v2), qz(v3)) << 16);
+            const uint8_t sb = (uint8_t)((__float_as_uint(s) >> 23) & 0xffu);
+            for (int p = 0; p < a.ep_world; ++p) {
+                *reinterpret_cast<uint32_t *>(a.ep_xq[p] + grow * a.D + b * 128 + 4 * lane) = q;
+                if (lane == 0) a.ep_xs[p][grow * nb + b] = sb;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // phase R: router logits of this CTA's expert rows (e = b + r*G), all tokens
 // ---------------------------------------------------------------------------
 __device__ void router_rows(const MoeArgs &a, uint8_t *scr, int G) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int E = a.E, D = a.D, T = a.T;
+    const int E = a.E, D = a.D, T = a.ep ? a.Tr : a.T;  // the tokens routed on this rank
     const int nrows = ((int)blockIdx.x < E) ? cdiv(E - (int)blockIdx.x, G) : 0;
     const int quarter = D / 4;  // warp w sums quarter w of every row
     double *part = reinterpret_cast<double *>(scr + R_PART);  // [warp][row][token]
@@ -693,6 +768,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
         bool dead = false;
         // everything below reads what the previous kernel on the stream wrote
         pdl_wait();
+        // expert parallelism: this forward's epoch (the previous one's finish advanced the counter)
+        const unsigned ep_epoch = a.ep ? __ldcg(a.ep_flags[a.ep_rank] + EP_CTR) + 1u : 0u;
         if (blockIdx.x == 0) {
             // this launch's h-ready counters start at zero (before the first barrier)
             const int ngr = p.nsg + min(a.El, a.T * a.topk) + cdiv(a.T * a.topk, NT);
@@ -700,23 +777,40 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
         }
         // ---- R: router logits of this CTA's rows; act_quant of tokens b, b + G, ...
         if (!a.given) router_rows(a, scr, G);
-        if (warp == 0) quantize_tokens_warp(a);
+        if (warp == 0) {
+            if (a.ep) quantize_tokens_ep(a);
+            else quantize_tokens_warp(a);
+        }
         if (!grid_barrier(f, a.err, a.wait_limit, G, flag)) dead = true;
-        // ---- S: top-k of tokens t = b mod G, one worker warp each
+        // ---- S: top-k of tokens t = b mod G, one worker warp each (expert
+        // parallelism: this rank's tokens, their routing written to every rank)
         if (!dead && !a.given) {
             float *sc_w = reinterpret_cast<float *>(scr + R_SC) + warp * MAX_E;
             int16_t *ridx_s = reinterpret_cast<int16_t *>(scr + R_RIDX);
             int16_t *pof_s = reinterpret_cast<int16_t *>(scr + R_POF);
             float *rw_s = reinterpret_cast<float *>(scr + R_RW);
-            for (int tk = blockIdx.x + warp * G; tk < a.T; tk += 4 * G) {
+            const int Tq = a.ep ? a.Tr : a.T;
+            for (int tk = blockIdx.x + warp * G; tk < Tq; tk += 4 * G) {
                 if (a.E <= 256) topk_token<8>(a, tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
                 else topk_token<MAX_E / 32>(a, tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
                 if (lane < a.topk) {
-                    a.ridx[tk * a.topk + lane] = ridx_s[tk * a.topk + lane];
-                    a.rw[tk * a.topk + lane] = rw_s[tk * a.topk + lane];
+                    const int e = ridx_s[tk * a.topk + lane];
+                    const float w = rw_s[tk * a.topk + lane];
+                    if (a.ep) {
+                        const size_t g = ((size_t)a.ep_rank * a.Tr + tk) * a.topk + lane;
+                        for (int pr = 0; pr < a.ep_world; ++pr) {
+                            a.ep_ridx[pr][g] = e;
+                            a.ep_rw[pr][g] = w;
+                        }
+                    } else {
+                        a.ridx[tk * a.topk + lane] = e;
+                        a.rw[tk * a.topk + lane] = w;
+                    }
                 }
             }
+            if (a.ep) __threadfence_system();
             if (!grid_barrier(f, a.err, a.wait_limit, G, flag)) dead = true;
+            if (!dead && a.ep && !ep_dispatch_handshake(a, ep_epoch, flag)) dead = true;
         }
         // ---- D: tables, then release the producer and the issuers
         if (!dead) build_tables(a, base, scr, misc);
@@ -732,7 +826,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
         if (!dead && ngroups == 0) {
             // no work at all (a routed-only call whose shard got no tokens): the
             // combine still writes every row block (zeros)
-            for (int rb = blockIdx.x; rb < D / 256; rb += G) combine_rows_v8<NWK>(a, rb * 256, 256, np_s, tp_s);
+            for (int rb = blockIdx.x; rb < D / 256; rb += G) {
+                combine_rows_v8<NWK>(a, rb * 256, 256, np_s, tp_s);
+                if (a.ep) ep_block_done(a, ep_epoch, D / 256, 2);
+            }
         }
 
         auto wwait = [&](uint64_t *bar, uint32_t parity) -> bool {
@@ -896,6 +993,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
                     __threadfence();
                     combine_rows_v8<NWK>(a, it.blk * 256, 256, np_s, tp_s);
                     if (tid == 0) a.cnt_rb[it.blk] = 0u;
+                    if (a.ep) ep_block_done(a, ep_epoch, D / 256, 1);
                 }
             }
         };
@@ -1047,6 +1145,39 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
     if (warp == W_PROD) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tm, 512);
+    }
+}
+
+// The owner's rows after expert parallelism over peer memory: wait (bounded) for
+// every rank's combine epoch, then y[t] = bf16(sum over ranks, in rank order, of
+// the partial rows the ranks wrote to this rank's receive buffer).
+__global__ void k_ep_finish(unsigned *flags, const float *yrecv, int P, int Tr, int D, __nv_bfloat16 *y,
+                            int *err, long long limit) {
+    __shared__ int ok;
+    const unsigned epoch = __ldcg(flags + EP_CTR) + 1u;
+    if (threadIdx.x == 0) {
+        bool good = true;
+        for (int p = 0; p < P && good; ++p)
+            good = spin_until(flags + EP_MAX_RANKS + p, epoch, err, limit, ld_acquire_sys_u32);
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;
+    const long long n = (long long)Tr * D;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        float acc = __ldcg(yrecv + i);
+        for (int p = 1; p < P; ++p) acc += __ldcg(yrecv + (long long)p * n + i);
+        y[i] = __float2bfloat16_rn(acc);
+    }
+    // the last block advances this rank's epoch counter (every block has read it)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(flags + EP_FIN, 1u) == gridDim.x - 1) {
+            flags[EP_FIN] = 0u;
+            __threadfence();
+            flags[EP_CTR] = epoch;
+        }
     }
 }
 

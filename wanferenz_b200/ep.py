@@ -116,3 +116,97 @@ def shard_range(n_experts, world, rank):
         raise ValueError(f"{n_experts} experts do not divide over {world} ranks")
     per = n_experts // world
     return rank * per, (rank + 1) * per
+
+
+class PeerGroup:
+    """Expert parallelism over peer memory for one layer (``wf_moe_forward_ep_p2p``).
+
+    Each rank allocates one buffer (set-up, ``wf_ep_alloc``), exports it with CUDA
+    IPC, and maps every other rank's; a forward then moves tokens, routing and
+    partial output rows over NVLink inside the fused kernel, with no NCCL call.
+    ``layer`` is this rank's shard (``n_local_experts = E / P``,
+    ``expert_offset = rank * n_local_experts``) whose ``max_tokens`` holds the
+    gathered batch (``P * T``).  Every rank must make the same sequence of
+    forwards, each on one stream.
+    """
+
+    def __init__(self, layer, group=None):
+        import ctypes
+
+        from . import _lib as L
+
+        self.lib = L.load()
+        self.layer = layer
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        nbytes = self.lib.wf_ep_buffer_bytes(ctypes.byref(layer.cfg), self.world)
+        if nbytes == 0:
+            raise ValueError(f"expert-parallel buffer: {self.lib.wf_last_error().decode()}")
+        own = ctypes.c_void_p()
+        L.check(self.lib.wf_ep_alloc(nbytes, ctypes.byref(own)), "wf_ep_alloc")
+        self._own = own
+        handle = (ctypes.c_uint8 * 64)()
+        L.check(self.lib.wf_ipc_get_handle(own, handle), "wf_ipc_get_handle")
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bufs = (ctypes.c_void_p * self.world)()
+        self._opened = []
+        for p in range(self.world):
+            if p == self.rank:
+                self.bufs[p] = own.value
+                continue
+            ptr = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[p])
+            L.check(self.lib.wf_ipc_open_handle(h, ctypes.byref(ptr)), "wf_ipc_open_handle")
+            self.bufs[p] = ptr.value
+            self._opened.append(ptr)
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def forward(self, x, input_ids=None, out=None, routing=False, out_routing=None):
+        """This rank's ``x [T, D]`` bf16 -> ``y [T, D]`` bf16 (and its routing when asked,
+        or into ``out_routing = (weights [T, k] f32, indices [T, k] int64)``)."""
+        import ctypes
+
+        from . import _lib as L
+
+        lay = self.layer
+        x = x.contiguous()
+        T = x.size(0)
+        if input_ids is not None:
+            input_ids = input_ids.reshape(-1).to(torch.int64).contiguous()
+        y = out if out is not None else torch.empty(T, lay.dim, dtype=torch.bfloat16, device=x.device)
+        rw = ri = None
+        if out_routing is not None:
+            rw, ri = out_routing
+        elif routing:
+            rw = torch.empty(T, lay.topk, dtype=torch.float32, device=x.device)
+            ri = torch.empty(T, lay.topk, dtype=torch.int64, device=x.device)
+        rc = self.lib.wf_moe_forward_ep_p2p(
+            ctypes.byref(lay.cfg), ctypes.byref(lay.wstruct), L.ptr(x), L.ptr(input_ids), T, self.rank, self.world,
+            self.bufs, L.ptr(y), L.ptr(rw), L.ptr(ri), L.ptr(lay.workspace), lay.workspace.numel(), L.stream_ptr())
+        L.check(rc, "wf_moe_forward_ep_p2p")
+        return (y, rw, ri) if routing else y
+
+    __call__ = forward
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (after every rank is done)."""
+        from . import _lib as L
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for ptr in self._opened:
+            L.check(self.lib.wf_ipc_close_handle(ptr), "wf_ipc_close_handle")
+        self._opened = []
+        if self._own is not None:
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            L.check(self.lib.wf_ep_free(self._own), "wf_ep_free")
+            self._own = None
