@@ -212,6 +212,51 @@ def test_checkpoint_loader_layer_matches_fixture_layer(tmp_path):
     cl.read_error()
 
 
+def _stand_in_moe(dl, spec):
+    """A module with the reference MoE's attributes (architecture.py:744-775), holding a
+    device layer's weights, for the plugin entry points on a GPU box without the reference."""
+    import types
+
+    w, I = dl.weights, spec.I
+
+    def lin(weight, scale, dt, sdt):
+        return types.SimpleNamespace(weight=weight.clone().view(dt), scale=scale.clone().view(sdt))
+
+    f4, e8 = torch.float4_e2m1fn_x2, torch.float8_e8m0fnu
+    experts = [types.SimpleNamespace(w1=lin(w.w13[e, :I], w.w13_s[e, :I], f4, e8),
+                                     w3=lin(w.w13[e, I:], w.w13_s[e, I:], f4, e8),
+                                     w2=lin(w.w2[e], w.w2_s[e], f4, e8), swiglu_limit=spec.swiglu_limit)
+               for e in range(spec.E)]
+    nb = I // 128
+    shared = types.SimpleNamespace(w1=lin(w.shared_w13[:I], w.shared_s13[:nb], torch.float8_e4m3fn, e8),
+                                   w3=lin(w.shared_w13[I:], w.shared_s13[nb:], torch.float8_e4m3fn, e8),
+                                   w2=lin(w.shared_w2, w.shared_s2, torch.float8_e4m3fn, e8))
+    gate = types.SimpleNamespace(weight=w.gate_w, bias=w.gate_b, tid2eid=w.tid2eid, hash=spec.hash_layer,
+                                 topk=spec.topk, score_func=spec.score_func, route_scale=spec.route_scale)
+    return types.SimpleNamespace(experts=experts, shared_experts=shared, gate=gate, dim=spec.D,
+                                 n_routed_experts=spec.E, experts_start_idx=0, experts_end_idx=spec.E)
+
+
+def test_drafter_install_runs_the_layer():
+    """install_drafter (decoding/expert_bank.py:167-196) on a drafter block: the patched
+    instance forward is the B200 layer forward (bit-identical) and counts its steps."""
+    import types
+
+    import wanferenz_b200.moe as b200
+
+    spec = F.LayerSpec(D=512, I=256, E=16, topk=6, score_func="sigmoid", route_scale=1.5, seed=92)
+    syn = _syn(spec)
+    dl = U.device_layer(syn, list(range(spec.E)))
+    moe = _stand_in_moe(dl, spec)
+    dstail = types.SimpleNamespace(mtp=[types.SimpleNamespace(ffn=moe)])
+    assert b200.install_drafter(dstail, mod=types.SimpleNamespace(world_size=1, scale_fmt="ue8m0")) == 1
+    x16, ids = syn.activations(5, draw=3)
+    x = U.bf16_tensor(x16)
+    y = moe.forward(x.view(1, 5, spec.D), torch.from_numpy(ids).cuda().view(1, 5))
+    assert torch.equal(y.view(5, spec.D), dl.forward(x))
+    assert moe._draft_steps == 1 and sorted(moe._grouped_bank) == ["w13", "w13_s", "w2", "w2_s"]
+
+
 def test_hash_duplicates_keep_one_contribution():
     """tid2eid rows like [3,3,7,3,12,7]: each expert contributes once (fp4_grouped.py:265-268)."""
     spec = F.LayerSpec(D=256, I=128, E=16, topk=6, score_func="sqrtsoftplus", hash_layer=True,

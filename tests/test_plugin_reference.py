@@ -200,6 +200,30 @@ def _child(ref_dir, q):
         moe._grouped_bank = None
         out["refusal_without_bank"] = decoder._moe_refusal(L, torch.device("cpu"), torch.bfloat16, ids, mod)
         b200.uninstall(mod)
+        # the drafter's MoE layers (decoding/expert_bank.py:167-196): instance-level
+        # forward on a load-time bank, the drafter's own tallies
+        import types as _types
+
+        spec, T, layer_id, _ = specs["sigmoid"]
+        dmoe, dlayer = _build_moe(mod, torch, spec, layer_id)
+        dstail = _types.SimpleNamespace(mtp=[_types.SimpleNamespace(ffn=dmoe), _types.SimpleNamespace(ffn=None)])
+
+        def host_layer(moe, m, preserve=True, max_tokens=64):
+            w, _ = b200.bank_from_module(moe, m, preserve=preserve)
+            return _types.SimpleNamespace(weights=w)
+
+        b200._layer_from_module = host_layer  # the device upload needs a GPU
+        out["drafter_took"] = b200.install_drafter(dstail, mod=mod)
+        x16, ids = dlayer.activations(3)
+        xd = torch.from_numpy(x16.view(np.int16)).view(torch.bfloat16).view(1, 3, spec.D)
+        with torch.no_grad():
+            y_draft = dmoe.forward(xd, torch.from_numpy(ids).view(1, 3))
+            y_ref = mod.MoE.forward(dmoe, xd, torch.from_numpy(ids).view(1, 3))
+        out["drafter_patched"] = isinstance(dmoe.forward, _types.MethodType) and getattr(
+            dmoe.forward.__func__, "_wf_b200", False)
+        out["drafter_steps"] = getattr(dmoe, "_draft_steps", 0)
+        out["drafter_same"] = bool(torch.equal(y_draft, y_ref))
+        out["drafter_bank"] = sorted((dmoe._grouped_bank or {}).keys())
         q.put(("ok", out))
     except Exception:
         q.put(("error", traceback.format_exc()))
@@ -241,6 +265,18 @@ def test_checkpoint_loader_matches_module_bank(results):
     for name in ("sigmoid", "hash", "rank1of2"):
         assert results[name]["checkpoint_bank_equal"], name
         assert results[name]["checkpoint_kwargs_equal"], name
+
+
+def test_drafter_layers_patched(results):
+    """install_drafter patches each drafter MoE instance (a block without an ffn is
+    skipped), gives it a load-time bank under the reference's keys and counts its
+    steps in the drafter's tally; the device step is replaced by the reference
+    forward here, so the output equals the reference's."""
+    assert results["drafter_took"] == 1
+    assert results["drafter_patched"]
+    assert results["drafter_steps"] == 1
+    assert results["drafter_same"]
+    assert results["drafter_bank"] == ["w13", "w13_s", "w2", "w2_s"]
 
 
 def test_config_fields_read_from_reference_module(results):

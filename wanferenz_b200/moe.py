@@ -475,6 +475,63 @@ def install(mod):
     return True
 
 
+def b200_draft_forward(self, x, input_ids):
+    """The drafter MoE's forward on the B200 kernels (decoding/expert_bank.py:108-164).
+
+    The reference's drafter path computes each (token, expert) pair on its own and
+    sums a token's experts in ascending id in fp32, then adds the shared expert:
+    ``MoE.forward``'s arithmetic, checked bit-exact by its own self-test
+    (expert_bank.py:261-344), for any number of draft tokens.  So this is the
+    layer forward itself, on the drafter layer's load-time bank, with the
+    drafter's tallies (``_draft_steps``, ``_draft_declined``); a configuration
+    the kernels do not cover runs the class forward, as the reference's decline
+    does (expert_bank.py:96-105)."""
+    try:
+        y = _b200_step(self, self._wf_layer, x, input_ids)
+    except WfUnsupported as e:
+        tally = getattr(self, "_draft_declined", None)
+        if tally is None:
+            tally = self._draft_declined = {}
+        tally[str(e)] = tally.get(str(e), 0) + 1
+        return type(self).forward(self, x, input_ids)
+    self._draft_steps = getattr(self, "_draft_steps", 0) + 1
+    return y
+
+
+b200_draft_forward._wf_b200 = True
+
+
+def install_drafter(dstail, mod=None, max_tokens=64):
+    """Routes the DSpark drafter's MoE layers through the B200 kernels
+    (``expert_bank.install_drafter``, decoding/expert_bank.py:167-196).
+
+    For every block of ``dstail.mtp`` whose ``ffn`` is an FP4 MoE with an FP8
+    shared expert, builds its load-time bank (the experts' parameters become
+    views into it, ``preserve=False``) and patches that instance's ``forward``.
+    Unlike the reference's drafter path, hash-routed layers are covered too.
+    Returns the number of layers patched."""
+    import types
+
+    global _MOD
+    if mod is not None:
+        _MOD = mod
+    took = 0
+    for blk in getattr(dstail, "mtp", ()):
+        moe = getattr(blk, "ffn", None)
+        if moe is None or not hasattr(moe, "experts_start_idx"):
+            continue
+        try:
+            _check_supported(moe)
+        except WfUnsupported:
+            continue
+        if getattr(moe, "_wf_layer", None) in (None, False):
+            moe._wf_layer = _layer_from_module(moe, _MOD, preserve=False, max_tokens=max_tokens)
+            moe._grouped_bank = _grouped_bank_of(moe._wf_layer)
+        moe.forward = types.MethodType(b200_draft_forward, moe)
+        took += 1
+    return took
+
+
 def uninstall(mod):
     global _REF_FORWARD
     if _REF_FORWARD is None:
