@@ -548,8 +548,10 @@ def run_gpu(args):
             extras["config4_T64_zipf"] = summary(stats(zl, 64, args.steps, args.warmup), 64)
             del zl
             torch.cuda.empty_cache()
-            # the FP8 block-scaled GEMM at M = 1 and 16
+            # the FP8 block-scaled GEMM at M = 1 and 16; the
+            # attention's dense projections on the same GEMM (model path, e8m0)
             extras["config3_fp8_gemm"] = fp8_gemm_points((1, 16), hbm)
+            extras["attention_fp8_projections"] = fp8_gemm_points((1, 16), hbm, ATTN_PROJECTIONS, ("e8m0",))
     # dominant kernel roofline
     kms = main["kms"]
     # the dominant HBM-bound kernel (multi-GPU: of the compute phases; the collectives
@@ -746,7 +748,15 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
-def fp8_gemm_points(Ms, hbm):
+# the attention's dense FP8 projections the reference routes to the same GEMM
+# (fp8_vector.py:505-513), (name, N, K)
+ATTN_PROJECTIONS = (("attn.wq_a", 1024, 4096), ("attn.wkv", 512, 4096), ("attn.wq_b", 32768, 1024),
+                    ("attn.wo_b", 4096, 8192), ("idx.wq_b", 8192, 1024))
+CONFIG3_SHAPES = (("config3", 4096, 4096), ("config3", 12288, 4096), ("config3", 4096, 16384),
+                  ("config3", 129280, 4096))
+
+
+def fp8_gemm_points(Ms, hbm, shapes=CONFIG3_SHAPES, kinds=("f32", "e8m0")):
     """``fp8_gemm`` (architecture.py:121-134 -> torch_ops.py:93-99) for
     the M in ``Ms`` and the four (N, K) of the model's dense projections, E4M3 weights
     with one fp32 (config 3) or e8m0 (model path) scale per 128x128 block, bf16
@@ -761,7 +771,7 @@ def fp8_gemm_points(Ms, hbm):
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     res = []
-    for (N, K) in ((4096, 4096), (12288, 4096), (4096, 16384), (129280, 4096)):
+    for (name, N, K) in shapes:
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         q, s8 = fp8_block_quant_torch(w)
         del w
@@ -772,6 +782,8 @@ def fp8_gemm_points(Ms, hbm):
         # f32: config 3 as stated (fp32 scales on both sides); e8m0: the model path
         # (scale_fmt="ue8m0", e8m0 scales on both sides, architecture.py:121-134)
         for kind, bs in (("f32", s32), ("e8m0", s8.view(torch.float8_e8m0fnu))):
+            if kind not in kinds:
+                continue
             for M in Ms:
                 x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
                 if kind == "f32":
@@ -800,7 +812,7 @@ def fp8_gemm_points(Ms, hbm):
                 del graph
                 nbytes = N * K + (N // 128) * (K // 128) * (4 if kind == "f32" else 1) + M * K * 2 + M * N * 2
                 gbs = nbytes / (us * 1e-6) / 1e9
-                res.append({"N": N, "K": K, "M": M, "scale": kind, "us": round(us, 2),
+                res.append({"shape": name, "N": N, "K": K, "M": M, "scale": kind, "us": round(us, 2),
                             "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
         del wqs, wq, q, s8, s32
         torch.cuda.empty_cache()
@@ -814,7 +826,9 @@ def run_fp8_gemm_suite(args):
     torch.cuda.set_device(0)
     hbm, peak_kind = peaks()
     res = fp8_gemm_points((1, 2, 4, 8, 16), hbm)
-    out = {"suite": "fp8_gemm", "metric": "FP8 block-scaled GEMM us/call (BASELINE config 3)",
+    res += fp8_gemm_points((1, 4, 16), hbm, ATTN_PROJECTIONS, ("e8m0",))
+    out = {"suite": "fp8_gemm", "metric": "FP8 block-scaled GEMM us/call (BASELINE config 3; the attention "
+                                          "projections of fp8_vector.py:505-513)",
            "unit": "us", "higher_is_better": False, "peak_GBps": hbm, "peak_kind": peak_kind,
            "timing": "CUDA graph of R calls over weight copies > L2, CUDA events", "results": res}
     print(json.dumps(out), flush=True)

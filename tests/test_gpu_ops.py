@@ -77,10 +77,13 @@ def test_fp4_gemm_golden(engine):
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 12288, 4096), (16, 4096, 4096), (5, 1024, 4096),
                                    (3, 512, 2048), (9, 2048, 1024), (4, 4096, 16384), (16, 1024, 8192),
-                                   (8, 129280, 4096), (1, 32768, 1024)])
+                                   (8, 129280, 4096), (1, 32768, 1024),
+                                   # the attention's dense projections (fp8_vector.py:505-513)
+                                   (1, 512, 4096), (16, 32768, 1024), (4, 4096, 8192), (1, 8192, 1024)])
 @pytest.mark.parametrize("scale", ["e8m0", "f32"])
 def test_fp8_gemm_vs_oracle(M, N, K, scale, engine):
-    """BASELINE config 3 shapes with K <= 4096 (fp32 weight scales per 128x128)."""
+    """BASELINE config 3 shapes and the attention projections of fp8_vector.py:505-513
+    (fp32 or e8m0 weight scales per 128x128)."""
     ops = _ops()
     a16 = F.normal_bf16((201, M, N, K), (M, K), 1.0)
     rng = F.rng(202, N, K)
