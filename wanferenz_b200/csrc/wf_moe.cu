@@ -1660,6 +1660,9 @@ int ensure_attrs() {
     cudaError_t e = cudaFuncSetAttribute((const void *)wf::tc::k_dense_tc,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, wf::tc::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc)");
+    e = cudaFuncSetAttribute((const void *)wf::tc::k_dense_tc_f32, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             wf::tc::F32_SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc f32)");
     e = cudaFuncSetAttribute((const void *)wf::fus::k_moe_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              wf::fus::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fused)");
@@ -2619,6 +2622,45 @@ static int dense(int wfmt, const void *a, const void *a_s, int a_kind, const voi
         if (e == cudaSuccess) counted();
         if (e == cudaSuccess) e = cudaGetLastError();
         return e == cudaSuccess ? WF_OK : cuda_fail(e, "tc gemm launch");
+    }
+    // tcgen05 with float32 block scales on both sides (fp8_gemm's scale_dtype float32):
+    // raw per-step products, scaled and summed in registers
+    const bool tc_f32 = !tc_disabled() && G == 0 && wfmt == wf::FMT_FP8 && a_kind == WF_SCALE_F32 &&
+                        b_kind == WF_SCALE_F32 && N % 128 == 0 && (K / nkc) <= wf::tc::KC_MAX &&
+                        ((uintptr_t)b % 32) == 0;
+    if (tc_f32) {
+        const int tnkc = tc_chunks(M, N, K, false);
+        const GemmWs Lt = gemm_ws_tc(M, N, K, tnkc);
+        if (ws_bytes < Lt.total) return fail(WF_E_ARG, "workspace too small (see wf_gemm_workspace_bytes)");
+        if (tnkc > 1 && gemm_shape_changed(ws, GemmShape{M, N, K, 16 + wfmt})) {
+            cudaError_t e0 = cudaMemsetAsync((uint8_t *)ws + Lt.cnt, 0, Lt.part - Lt.cnt, st);
+            if (e0 != cudaSuccess) return cuda_fail(e0, "cudaMemsetAsync(gemm counters)");
+        }
+        wf::tc::DenseF32Args t;
+        memset(&t, 0, sizeof(t));
+        rc = weight_tensor_map(&t.tmA, b, false, (uint64_t)N, (uint64_t)K);
+        if (rc) return rc;
+        t.a = (const uint8_t *)a; t.a_s = (const float *)a_s; t.w_s = (const float *)b_s;
+        t.M = (int)M; t.N = (int)N; t.K = (int)K; t.nkc = tnkc; t.Kc = (int)(K / tnkc);
+        t.out = (__nv_bfloat16 *)out; t.err = (int *)ws;
+        t.cnt = (unsigned *)((uint8_t *)ws + Lt.cnt);
+        t.part = (float *)((uint8_t *)ws + Lt.part);
+        const int G_ = sm_count();
+        if (G_ <= 0) return fail(WF_E_CUDA, "no CUDA device");
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(G_);
+        lc.blockDim = dim3(wf::tc::THREADS);
+        lc.dynamicSmemBytes = wf::tc::F32_SMEM;
+        lc.stream = st;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&lc, wf::tc::k_dense_tc_f32, t);
+        if (e == cudaSuccess) counted();
+        if (e == cudaSuccess) e = cudaGetLastError();
+        return e == cudaSuccess ? WF_OK : cuda_fail(e, "tc f32 gemm launch");
     }
     wf::DenseArgs d;
     d.M = (int)M; d.N = (int)N; d.K = (int)K; d.G = (int)G;

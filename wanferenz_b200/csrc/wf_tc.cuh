@@ -472,5 +472,218 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same GEMM with float32 block scales (fp8_gemm with scale_dtype float32,
+// torch_ops.py:93-99): the tensor cores cannot apply a non-power-of-two scale, so
+// each 128-wide K step's product goes into a fresh TMEM accumulator (unit UE8M0
+// scales) and the worker warps add sa[m, kb] * sw[n / 128, kb] * D_step to fp32
+// registers, in K order.  E4M3 weights only; ring of NACC step accumulators.
+// ---------------------------------------------------------------------------
+constexpr int NACC = 8;                      // step accumulators in flight
+constexpr uint32_t COL_ACC = 0;              // NACC x 16 columns
+constexpr uint32_t COL_UNIT = 128;           // unit scale factors (4 columns)
+constexpr int F32_NBAR = 2 * STAGES + 2 + 2 * NACC + 1;  // ..., fin
+constexpr int F32_OFF_SA = OFF_BAR + F32_NBAR * 8 + 64;  // [NTOK][KC_MAX / 128] f32 activation scales
+constexpr int F32_SMEM = F32_OFF_SA + NTOK * (KC_MAX / 128) * 4 + 1024;
+static_assert(F32_SMEM <= 232448, "shared memory budget");
+
+struct DenseF32Args {
+    CUtensorMap tmA;     // weights e4m3 [N, K], box 128 x 128, 128-byte swizzle
+    const uint8_t *a;    // e4m3 tokens [M, K]
+    const float *a_s;    // [M, K/128]
+    const float *w_s;    // [ceil(N/128), K/128]
+    int M, N, K, nkc, Kc;
+    __nv_bfloat16 *out;  // [M, N]
+    float *part;         // [nkc, M, N] (nkc > 1)
+    unsigned *cnt;       // (nkc > 1)
+    int *err;
+};
+
+__global__ void __launch_bounds__(THREADS, 1) k_dense_tc_f32(const __grid_constant__ DenseF32Args d) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bar = reinterpret_cast<uint64_t *>(base + OFF_BAR);
+    uint64_t *full = bar, *empty = bar + STAGES, *b_ready = bar + 2 * STAGES, *b_free = bar + 2 * STAGES + 1;
+    uint64_t *acc_ready = bar + 2 * STAGES + 2, *acc_free = bar + 2 * STAGES + 2 + NACC;
+    uint64_t *fin = bar + 2 * STAGES + 2 + 2 * NACC;
+    uint32_t *tmem_base = reinterpret_cast<uint32_t *>(bar + F32_NBAR);
+    volatile int *abort = reinterpret_cast<volatile int *>(bar + F32_NBAR) + 1;
+    float *sa_s = reinterpret_cast<float *>(base + F32_OFF_SA);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+        mbar_init(b_ready, 4);
+        mbar_init(b_free, 1);
+        for (int j = 0; j < NACC; ++j) { mbar_init(acc_ready + j, 1); mbar_init(acc_free + j, 4); }
+        mbar_init(fin, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == W_MMA) { tmem_alloc(tmem_base, 256); tmem_relinquish(); }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tm = *tmem_base;
+    const int ntile = d.N / 128, ntg = (d.M + NTOK - 1) / NTOK;
+    const int n = d.nkc * ntg * ntile;
+    const int i0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
+    const int i1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
+    const int nks = d.Kc / 128;
+    uint8_t *Bsm = base + OFF_B;
+    DenseArgs geo;  // item decoding only
+    geo.M = d.M; geo.N = d.N; geo.nkc = d.nkc;
+
+    if (warp == W_PROD) {
+        if (lane == 0) {
+            int gs = 0;
+            for (int i = i0; i < i1 && !*abort; ++i) {
+                const DItem it = dense_item(geo, i);
+                for (int s = 0; s < nks; ++s, ++gs) {
+                    const int st = gs % STAGES;
+                    if (gs == STAGES) pdl_wait();
+                    if (gs >= STAGES && !twait(empty + st, ((gs / STAGES) - 1) & 1, d.err, abort)) break;
+                    mbar_arrive_expect_tx(full + st, ABOX);
+                    tma_load_2d(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, full + st);
+                }
+            }
+        }
+    } else if (warp == W_MMA) {
+        if (lane == 0) {
+            pdl_wait();
+            int gs = 0, nb = 0, key = -1;
+            for (int i = i0; i < i1 && !*abort; ++i) {
+                const DItem it = dense_item(geo, i);
+                if (it.key != key) {
+                    if (!twait(b_ready, nb & 1, d.err, abort)) break;
+                    ++nb;
+                    key = it.key;
+                }
+                bool ok = true;
+                for (int s = 0; s < nks; ++s, ++gs) {
+                    const int st = gs % STAGES, ab = gs % NACC;
+                    if (gs >= NACC && !twait(acc_free + ab, ((gs / NACC) - 1) & 1, d.err, abort)) { ok = false; break; }
+                    if (!twait(full + st, (gs / STAGES) & 1, d.err, abort)) { ok = false; break; }
+                    fence_after_sync();
+                    const uint64_t ad = smem_desc_sw128(base + st * ABOX);
+                    const uint64_t bd = smem_desc_sw128(Bsm + s * BSTEP);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        mma_mxf8f6f4(tm + COL_ACC + 16 * ab, ad + 2 * j, bd + 2 * j, idesc_mxf8f6f4(0, 0, NTOK, j),
+                                     tm + COL_UNIT, tm + COL_UNIT, j != 0);
+                    commit(empty + st);
+                    commit(acc_ready + ab);
+                }
+                if (!ok) break;
+                const bool last_of_set = (i + 1 >= i1) || dense_item(geo, i + 1).key != it.key;
+                if (last_of_set) commit(b_free);
+            }
+            // all of this thread's MMAs complete before TMEM is released
+            commit(fin);
+            wf_wait(fin, 0, d.err);
+        }
+    } else {
+        pdl_wait();
+        const int wq = warp & 3;
+        const int wt = threadIdx.x - W_WORK0 * 32;
+        const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
+        const int K = d.K, kb_all = K / 128;
+        // unit scale factors (2^0) for both operands, every lane
+        tmem_st4(tm + lane_base + COL_UNIT, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+        tmem_wait_st();
+        fence_before_sync();
+        int nb = 0, key = -1, gs = 0;
+        bool dead = false;
+        for (int i = i0; i < i1 && !dead; ++i) {
+            if (*abort) break;
+            const DItem it = dense_item(geo, i);
+            if (it.key != key) {
+                if (nb > 0 && !twait(b_free, (nb - 1) & 1, d.err, abort)) break;
+                const int row = wt >> 3, chunk = wt & 7;
+                const bool rv = row < it.ntok;
+                const uint8_t *src = d.a + (size_t)(it.tok0 + (rv ? row : 0)) * K + (size_t)it.kc * d.Kc + chunk * 16;
+                for (int s0 = 0; s0 < nks; s0 += 8) {
+                    uint4 v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        v[u] = (rv && s0 + u < nks) ? ldg128(src + (s0 + u) * 128) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (s0 + u < nks)
+                            *reinterpret_cast<uint4 *>(Bsm + (s0 + u) * BSTEP + sw128_offset(row, chunk)) = v[u];
+                }
+                // the token group's activation scales of this K chunk
+                bar_sync(1, 128);  // the previous group's epilogue read sa_s
+                for (int k = wt; k < NTOK * nks; k += 128) {
+                    const int m = k / nks, s = k - m * nks;
+                    sa_s[k] = m < it.ntok ? __ldg(d.a_s + (size_t)(it.tok0 + m) * kb_all + it.kc * nks + s) : 0.f;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                bar_sync(1, 128);
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b_ready);
+                ++nb;
+                key = it.key;
+            }
+            const int row = it.tile * 128 + 32 * wq + lane;
+            float acc[NTOK];
+#pragma unroll
+            for (int m = 0; m < NTOK; ++m) acc[m] = 0.f;
+            for (int s = 0; s < nks; ++s, ++gs) {
+                const int ab = gs % NACC;
+                const float sw = __ldg(d.w_s + (size_t)(row / 128) * kb_all + it.kc * nks + s);
+                if (!twait(acc_ready + ab, (gs / NACC) & 1, d.err, abort)) { dead = true; break; }
+                fence_after_sync();
+                uint32_t v[16];
+                tmem_ld16(tm + lane_base + COL_ACC + 16 * ab, v);
+                tmem_wait_ld();
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_free + ab);
+#pragma unroll
+                for (int m = 0; m < NTOK; ++m) acc[m] += (sa_s[m * nks + s] * sw) * __uint_as_float(v[m]);
+            }
+            if (dead) break;
+            if (d.nkc == 1) {
+#pragma unroll
+                for (int m = 0; m < NTOK; ++m)
+                    if (m < it.ntok) d.out[(size_t)(it.tok0 + m) * d.N + row] = __float2bfloat16_rn(acc[m]);
+            } else {
+#pragma unroll
+                for (int m = 0; m < NTOK; ++m)
+                    if (m < it.ntok) d.part[((size_t)it.kc * d.M + it.tok0 + m) * d.N + row] = acc[m];
+                __threadfence();
+                __syncwarp();
+                unsigned *cnt = d.cnt + ((size_t)it.tg * ntile + it.tile) * 4 + wq;
+                int last = 0;
+                if (lane == 0) last = atomicAdd(cnt, 1u) == (unsigned)d.nkc - 1;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    float sum[NTOK];
+#pragma unroll
+                    for (int m = 0; m < NTOK; ++m) sum[m] = 0.f;
+                    for (int c = 0; c < d.nkc; ++c) {
+                        const float *pc = d.part + ((size_t)c * d.M + it.tok0) * d.N + row;
+#pragma unroll
+                        for (int m = 0; m < NTOK; ++m) sum[m] += m < it.ntok ? __ldcg(pc + (size_t)m * d.N) : 0.f;
+                    }
+#pragma unroll
+                    for (int m = 0; m < NTOK; ++m)
+                        if (m < it.ntok) d.out[(size_t)(it.tok0 + m) * d.N + row] = __float2bfloat16_rn(sum[m]);
+                    if (lane == 0) *cnt = 0u;
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == W_MMA) {
+        fence_after_sync();
+        tmem_dealloc(tm, 256);
+    }
+}
+
 }  // namespace tc
 }  // namespace wf
