@@ -244,8 +244,8 @@ def tc_engine():
 
 
 def fused_engine():
-    """On tcgen05 the whole layer is one launch unless WF_FUSED=0."""
-    return tc_engine() and os.environ.get("WF_FUSED", "1") != "0"
+    """On tcgen05 the whole layer is one launch when WF_FUSED=1 (three launches otherwise)."""
+    return tc_engine() and os.environ.get("WF_FUSED", "0") not in ("", "0")
 
 
 def kernel_names():

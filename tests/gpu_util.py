@@ -236,11 +236,13 @@ def _elem_ok(y, ref, floor):
     return bool((np.abs(y - ref) / np.maximum(np.abs(ref), floor) <= 1e-2).all())
 
 
-def requant_alternatives(x_row, terms, ue8m0=True, limit=0.0, window=8):
+def requant_alternatives(x_row, terms, ue8m0=True, limit=0.0, window=64, window_h=16):
     """Outputs of one token under the exact chain (fp64 sums rounded to fp32) and,
-    for every gate / up / h / expert-output value within ``window`` fp32 ulps of a
-    bf16 rounding midpoint, the chain with that one value rounded to its other bf16
-    neighbour.
+    for every gate / up / expert-output value within ``window`` fp32 ulps of a bf16
+    rounding midpoint (a K = 4096 fp32 sum routinely lands tens of ulps from the
+    exact one) and every h value within ``window_h`` ulps (a few fp32 operations
+    after the gate and up values), the chain with that one value rounded to its
+    other bf16 neighbour.
 
     ``terms``: the token's experts in the reference's summation order (routed in
     ascending id, then the shared expert), each ``(w1, w3, w2 dequantized float32
@@ -257,9 +259,9 @@ def requant_alternatives(x_row, terms, ue8m0=True, limit=0.0, window=8):
         aa = (q * s.repeat_interleave(128, -1)).to(torch.float64)
         return (aa @ w.to(torch.float64).T).to(torch.float32)
 
-    def near(v32):
+    def near(v32, win=window):
         low = (v32.view(torch.int32) & 0xFFFF).to(torch.int64)
-        return torch.nonzero((low - 0x8000).abs() <= window).flatten().tolist()
+        return torch.nonzero((low - 0x8000).abs() <= win).flatten().tolist()
 
     def other(v32, i):  # the other bf16 neighbour of v32[i]
         b = bf16(v32[:, i:i + 1])
@@ -287,7 +289,7 @@ def requant_alternatives(x_row, terms, ue8m0=True, limit=0.0, window=8):
         o = bf16(o32)
         if flip and flip[0] == "o":
             o[:, flip[1]] = other(o32, flip[1])
-        return o, (near(g32), near(u32), near(pre), near(o32))
+        return o, (near(g32), near(u32), near(pre, window_h), near(o32))
 
     base, cands = [], []
     for k, (w1, w3, w2, wt) in enumerate(terms):

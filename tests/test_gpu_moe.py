@@ -49,10 +49,10 @@ def _layer(spec, touched, **kw):
 
 @pytest.fixture(params=["fused", "tcgen05", "mma_sync"])
 def engine(request, monkeypatch):
-    """Every layer engine: the single-launch tcgen05 layer (default where scales are
-    e8m0), the three-launch tcgen05 one (WF_FUSED=0) and the mma.sync one."""
+    """Every layer engine: the three-launch tcgen05 one (default where scales are
+    e8m0), the single-launch tcgen05 layer (WF_FUSED=1) and the mma.sync one."""
     monkeypatch.setenv("WF_DISABLE_TC", "1" if request.param == "mma_sync" else "0")
-    monkeypatch.setenv("WF_FUSED", "0" if request.param == "tcgen05" else "1")
+    monkeypatch.setenv("WF_FUSED", "1" if request.param == "fused" else "0")
     return request.param
 
 

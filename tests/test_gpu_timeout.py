@@ -25,7 +25,7 @@ SPEC = F.LayerSpec(D=512, I=256, E=16, topk=4, score_func="sigmoid", route_scale
 @pytest.fixture(params=["fused", "tcgen05", "mma_sync"])
 def engine(request, monkeypatch):
     monkeypatch.setenv("WF_DISABLE_TC", "1" if request.param == "mma_sync" else "0")
-    monkeypatch.setenv("WF_FUSED", "0" if request.param == "tcgen05" else "1")
+    monkeypatch.setenv("WF_FUSED", "1" if request.param == "fused" else "0")
     return request.param
 
 

@@ -1759,11 +1759,12 @@ bool tc_disabled() {
     return v && v[0] && v[0] != '0';
 }
 
-// WF_FUSED=0 runs the tcgen05 expert phases as three launches (router, w1/w3,
-// w2) instead of the single fused launch.
-bool fused_disabled() {
+// WF_FUSED=1 runs the whole layer as the single fused launch (wf_moe_fused.cuh)
+// instead of three launches (router, w1/w3, w2); expert parallelism over peer
+// memory always uses the fused launch.
+bool fused_requested() {
     const char *v = getenv("WF_FUSED");
-    return v && v[0] == '0';
+    return v && v[0] && v[0] != '0';
 }
 
 // smem row stride: row bytes rounded up to 128, plus 16 (FP4: a warp reads one
@@ -1898,7 +1899,8 @@ wf::Geo make_geo(int D, int I) {
 // Expert phases on tcgen05: needs power-of-two (e8m0) activation and shared
 // scales, 256-row output blocks, the tcgen05 workspace, aligned weight banks.
 int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, uint8_t *b,
-            size_t ws_bytes, wf::MoeArgs &a, wf::mtc::TcArgs *t, wf::fus::FArgs *f = nullptr) {
+            size_t ws_bytes, wf::MoeArgs &a, wf::mtc::TcArgs *t, wf::fus::FArgs *f = nullptr,
+            bool force_fused = false) {
     a.tc = 0;
     if (f) f->gbar = nullptr;
     if (!t || tc_disabled()) return WF_OK;
@@ -1939,7 +1941,7 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
     t->sq = b + L.sq; t->sqs = b + L.sqs;
     t->part = (float *)(b + L.part);
     t->cnt = (unsigned *)(b + L.cnt_tc);
-    if (f && !fused_disabled() && ws_bytes >= L.total_fused) {
+    if (f && (force_fused || fused_requested()) && ws_bytes >= L.total_fused) {
         f->gbar = (unsigned long long *)(b + L.fgbar);
         f->hcnt = (unsigned *)(b + L.fhcnt);
         f->cnt = (unsigned *)(b + L.fcnt);
@@ -1955,7 +1957,7 @@ int fill_tc(const wf_moe_config *c, const wf_moe_weights *w, const WsLayout &L, 
 int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
               const int64_t *ids, int T, void *ws, size_t ws_bytes, wf::MoeArgs &a,
               wf::mtc::TcArgs *t = nullptr, bool routing_given = false, bool tc_counters = true,
-              wf::fus::FArgs *f = nullptr) {
+              wf::fus::FArgs *f = nullptr, bool force_fused = false) {
     int rc = check_cfg(c);
     if (rc) return rc;
     if (!w || !x || !ws) return fail(WF_E_ARG, "null weights, input or workspace");
@@ -1998,7 +2000,7 @@ int fill_args(const wf_moe_config *c, const wf_moe_weights *w, const void *x,
     a.cnt_rb = (unsigned *)(b + L.cnt_rb);
     a.err = (int *)(b + L.err);
     a.g = make_geo(a.D, a.I);
-    return fill_tc(c, w, L, b, ws_bytes, a, t, f);
+    return fill_tc(c, w, L, b, ws_bytes, a, t, f, force_fused);
 }
 
 }  // namespace
@@ -2289,11 +2291,11 @@ int wf_moe_forward_ep_p2p(const wf_moe_config *cfg, const wf_moe_weights *w, con
     wf::MoeArgs a;
     wf::mtc::TcArgs t;
     wf::fus::FArgs f;
-    rc = fill_args(cfg, w, x, input_ids, T * world, workspace, workspace_bytes, a, &t, false, true, &f);
+    rc = fill_args(cfg, w, x, input_ids, T * world, workspace, workspace_bytes, a, &t, false, true, &f, true);
     if (rc) return rc;
     if (!a.tc || !f.gbar)
         return fail(WF_E_ARG, "expert parallelism over peer memory needs the fused tcgen05 engine "
-                              "(e8m0 scales, the full workspace, WF_FUSED unset)");
+                              "(e8m0 scales, the full workspace, WF_DISABLE_TC unset)");
     const EpLayout E = ep_layout(cfg, world);
     a.ep = 1; a.ep_rank = rank; a.ep_world = world; a.Tr = T;
     for (int p = 0; p < world; ++p) {
