@@ -71,7 +71,7 @@ def parse():
                     help="skip the config-3 and config-4 sub-results of the default line")
     ap.add_argument("--suite", default="moe", choices=("moe", "fp8_gemm"),
                     help="fp8_gemm: BASELINE config 3, the FP8 block-scaled GEMM sweep (one JSON line, N=1)")
-    ap.add_argument("--ep", default="p2p", choices=("p2p", "nccl"),
+    ap.add_argument("--ep", default="nccl", choices=("p2p", "nccl"),
                     help="N > 1: p2p = tokens, routing and partial rows moved over NVLink by the fused kernel "
                          "(wf_moe_forward_ep_p2p); nccl = route, NCCL all-gather, expert forward, NCCL combine")
     ap.add_argument("--combine", default="reduce_scatter", choices=("reduce_scatter", "all_to_all"),

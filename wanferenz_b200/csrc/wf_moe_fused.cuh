@@ -647,6 +647,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
     if (warp == W_PROD) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
+            const uint64_t pol = tc::policy_evict_first();
             Cur cur;
             Seg sg{0, 0, 0, 0, -1};
             int gs = 0, st = 0, lap = 0;
@@ -668,11 +669,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
                     uint8_t *dst = base + st * STAGE_BYTES;
                     mbar_arrive_expect_tx(B.full + st, tx);
                     if (ph2) {
-                        if (it.shared) tc::tma_load_3d(dst, &t.m_s13, j * 128, it.blk * 128, 0, B.full + st);
-                        else tc::tma_load_3d(dst, &t.m_r13, j * 128, it.blk * 128, 2 * it.el, B.full + st);
+                        if (it.shared) tc::tma_load_3d_hint(dst, &t.m_s13, j * 128, it.blk * 128, 0, B.full + st, pol);
+                        else tc::tma_load_3d_hint(dst, &t.m_r13, j * 128, it.blk * 128, 2 * it.el, B.full + st, pol);
                     } else {
-                        if (it.shared) tc::tma_load_2d(dst, &t.m_s2, j * 128, it.blk * 256, B.full + st);
-                        else tc::tma_load_2d(dst, &t.m_r2, j * 128, it.el * D + it.blk * 256, B.full + st);
+                        if (it.shared) tc::tma_load_2d_hint(dst, &t.m_s2, j * 128, it.blk * 256, B.full + st, pol);
+                        else tc::tma_load_2d_hint(dst, &t.m_r2, j * 128, it.el * D + it.blk * 256, B.full + st, pol);
                     }
                 }
                 if (!ok) break;

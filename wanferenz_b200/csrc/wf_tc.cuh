@@ -113,6 +113,34 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// L2 policy for streamed weights: evict first, so a layer step's ~1 GB of weights
+// passing through the 126 MB L2 does not displace the kernels' instructions, the
+// routing tables and the activations, which are read again.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// tma_load_2d / tma_load_3d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_hint(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar,
+                                                 uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                                 uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // Prefetch one 2D box of the tensor map into L2 (no shared memory, no completion).
 __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
@@ -279,6 +307,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
 
     if (warp == W_PROD) {
         if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
             int gs = 0;
             for (int i = i0; i < i1 && !*B.abort; ++i) {
                 const DItem it = dense_item(d, i);
@@ -289,7 +318,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc(const __grid_constant__
                     if (gs == STAGES) pdl_wait();
                     if (gs >= STAGES && !twait(B.empty + st, ((gs / STAGES) - 1) & 1, d.err, B.abort)) break;
                     mbar_arrive_expect_tx(B.full + st, d.fp4 ? ABOX / 2 : ABOX);
-                    tma_load_2d(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, B.full + st);
+                    tma_load_2d_hint(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, B.full + st,
+                                     pol);
                 }
             }
         }
@@ -536,6 +566,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc_f32(const __grid_consta
 
     if (warp == W_PROD) {
         if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
             int gs = 0;
             for (int i = i0; i < i1 && !*abort; ++i) {
                 const DItem it = dense_item(geo, i);
@@ -544,7 +575,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_dense_tc_f32(const __grid_consta
                     if (gs == STAGES) pdl_wait();
                     if (gs >= STAGES && !twait(empty + st, ((gs / STAGES) - 1) & 1, d.err, abort)) break;
                     mbar_arrive_expect_tx(full + st, ABOX);
-                    tma_load_2d(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, full + st);
+                    tma_load_2d_hint(base + st * ABOX, &d.tmA, it.kc * d.Kc + s * 128, it.tile * 128, full + st,
+                                     pol);
                 }
             }
         }
