@@ -257,8 +257,8 @@ def kernel_names():
 
 
 # ncu traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the tcgen05
-# expert phases, 16 tokens, uniform routing: profiles/k_moe_tc_config2_T16.md
-MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 763.3e6, "k_moe_tc<3>": 387.5e6}
+# expert phases, 16 tokens, uniform routing: profiles/moe_layer_launches_config2_T16.md
+MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 728.9e6, "k_moe_tc<3>": 366.5e6}
 
 
 def step_bytes(indices, T, e0, El, router=True, shared=True):
@@ -565,7 +565,7 @@ def run_gpu(args):
     if dom in MEASURED_TRAFFIC_T16 and T == 16 and world == 1 and args.routing == "uniform":
         traffic = MEASURED_TRAFFIC_T16[dom]
         traffic_src = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload "
-                       "(1 layer, random FP4 bytes): profiles/k_moe_tc_config2_T16.md")
+                       "(1 layer, random FP4 bytes): profiles/moe_layer_launches_config2_T16.md")
 
     e2e = None
     if not args.no_e2e:

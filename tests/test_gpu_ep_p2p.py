@@ -4,8 +4,8 @@
   buffer, partial rows through its receive buffer, the finish kernel) gives
   outputs bit-identical to the regular fused forward, eagerly and replayed from
   a CUDA graph (the hand-off epochs are counted on the device).
-* Two ranks, one process per GPU (skipped with fewer than two GPUs): each rank
-  holds half of the experts and its own tokens; every rank's output meets the
+* Two and four ranks, one process per GPU (skipped with fewer GPUs): each rank
+  holds its share of the experts and its own tokens; every rank's output meets the
   layer tolerance against the single-process oracle (architecture.py:777-794).
 """
 
@@ -113,12 +113,12 @@ def _rank_main(rank, world, port, T, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("T", [3, 16])
-def test_two_ranks_match_oracle(T):
+@pytest.mark.parametrize("world,T", [(2, 3), (2, 16), (4, 5)])
+def test_ranks_match_oracle(world, T):
     import torch.multiprocessing as mp
 
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -138,8 +138,8 @@ def test_two_ranks_match_oracle(T):
     for call in range(3):
         y = np.concatenate([res[r][call][0] for r in range(world)])
         ri = np.concatenate([res[r][call][2] for r in range(world)])
-        tie = U.near_tie_rows(xf, syn, what=f"two ranks T={T}")
+        tie = U.near_tie_rows(xf, syn, what=f"{world} ranks T={T}")
         np.testing.assert_array_equal(ri[~tie], i_ref[~tie])
-        U.assert_layer_close_envelope(y[~tie], y_ref[~tie], y_ref32[~tie], f"two ranks T={T} call {call}")
+        U.assert_layer_close_envelope(y[~tie], y_ref[~tie], y_ref32[~tie], f"{world} ranks T={T} call {call}")
         if call:
             assert np.array_equal(y, np.concatenate([res[r][0][0] for r in range(world)])), "calls differ"
