@@ -2,24 +2,23 @@
 
 Every wait of the layer kernels on another role's progress is bounded.  The
 test lowers that bound (``wf_set_wait_limit``) to a few hundred SM cycles, far
-below the microseconds a weight stage or an operand takes to arrive, so some
-wait runs out.  The kernels must then wind down (the drains of their own
-copies and MMAs keep the long bound), set WF_E_TIMEOUT in the workspace's
-error word, and leave the context usable: with the default bound restored
-and the workspace re-zeroed, the next forward is correct.
+below the microseconds a weight stage or an operand takes to arrive.  The
+layer has the BASELINE config-1 shape, so every CTA streams many more weight
+stages than its ring holds: some role must wait for a refill, and that wait
+runs out.  The kernels must then wind down (the drains of their own copies and
+MMAs keep the long bound), set WF_E_TIMEOUT in the workspace's error word, and
+leave the context usable: with the default bound restored and the workspace
+re-zeroed, the next forward is bit-identical to a forward run before the
+timeout.
 """
 
-import numpy as np
 import pytest
 import torch
 
 from oracle import fixtures as F
-from oracle import moe_oracle as O
 from tests import gpu_util as U
 
 pytestmark = pytest.mark.gpu
-
-SPEC = F.LayerSpec(D=512, I=256, E=16, topk=4, score_func="sigmoid", route_scale=1.5, seed=71)
 
 
 @pytest.fixture(params=["fused", "tcgen05", "mma_sync"])
@@ -34,12 +33,15 @@ def test_short_wait_limit_reports_timeout_and_context_recovers(engine):
     from wanferenz_b200.moe import MoELayer  # noqa: F401  (loads the library)
 
     lib = L.load()
-    syn = F.SyntheticLayer(SPEC)
+    syn = F.SyntheticLayer(F.CONFIG1)
     T = 8
-    x16, ids = syn.activations(T, draw=1)
-    y_ref, _, i_ref = O.moe_forward(O.bf16_to_f32(x16), syn.params(), ids)
-    layer = U.device_layer(syn, np.unique(i_ref), max_tokens=16)
+    x16, _ = syn.activations(T, draw=1)
+    layer = U.device_layer(syn, [], max_tokens=16)  # routed experts: random FP4 bytes
     x = U.bf16_tensor(x16)
+    y0, w0, i0 = layer.forward(x, routing=True)
+    torch.cuda.synchronize()
+    layer.read_error()
+    assert torch.isfinite(y0.float()).all()
     try:
         L.check(lib.wf_set_wait_limit(200), "wf_set_wait_limit")
         layer.forward(x)
@@ -47,11 +49,11 @@ def test_short_wait_limit_reports_timeout_and_context_recovers(engine):
         rc = lib.wf_moe_read_error(L.ptr(layer.workspace), layer.workspace.numel(), L.stream_ptr())
     finally:
         lib.wf_set_wait_limit(0)
-    assert rc == L.WF_E_TIMEOUT, f"expected a timed-out wait, got status {rc}"
-    # the context is intact: default bound, fresh workspace, correct output
+    assert rc == L.WF_E_TIMEOUT, f"{engine}: expected a timed-out wait, got status {rc}"
+    # the context is intact: default bound, fresh workspace, the same output as before
     layer.workspace.zero_()
-    y, _, ri = layer.forward(x, routing=True)
+    y, w, i = layer.forward(x, routing=True)
     torch.cuda.synchronize()
     layer.read_error()
-    np.testing.assert_array_equal(ri.cpu().numpy(), i_ref)
-    U.assert_layer_close(U.to_f32(y), y_ref, f"{engine} after a timeout")
+    assert torch.equal(i, i0) and torch.equal(w, w0), f"{engine}: routing differs after a timeout"
+    assert torch.equal(y, y0), f"{engine}: output differs after a timeout"
