@@ -706,97 +706,146 @@ __device__ __forceinline__ float red_sum(const float *red, int arow, int tok) {
 }
 
 // ---------------------------------------------------------------------------
-// router (K1, consumer warps): logits[t][e] = sum_k x[t][k] w[e][k] in fp64
+// router (K1, consumer warps)
 // ---------------------------------------------------------------------------
-__device__ void router_logits(const MoeArgs &a, const Smem &sm, const __nv_bfloat16 *xsm) {
-    constexpr int RTP = 4;  // tokens per pass
-    constexpr int KU = 4;   // 256-element chunks of a lane per quarter row (D <= 4096)
+constexpr int RKE = 2;  // 8-element chunks of a lane per gate row and K-eighth (D <= 4096)
+
+// The gate weights a consumer warp multiplies in router pass p: K-eighth `warp`
+// of the pass's two rows, as raw bf16 pairs.
+struct GateChunk {
+    uint4 w[2][RKE];
+};
+
+__device__ __forceinline__ GateChunk load_gate_chunk(const MoeArgs &a, int p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const int nrows = (blockIdx.x < a.E) ? cdiv(a.E - blockIdx.x, G) : 0;
+    const int eighth = a.D / 8;
+    GateChunk c;
+#pragma unroll
+    for (int rl = 0; rl < 2; ++rl) {
+        const int r = p + rl;
+        const bool rv = r < nrows;
+        const __nv_bfloat16 *wrow = a.gate_w + (size_t)(rv ? blockIdx.x + r * G : 0) * a.D + warp * eighth;
+#pragma unroll
+        for (int u = 0; u < RKE; ++u) {
+            const int k = lane * 8 + u * 256;
+            c.w[rl][u] = (rv && k < eighth) ? ldg128(wrow + k) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    return c;
+}
+
+// Router logits, logits[t][e] = sum_k x[t][k] w[e][k] (Gate.forward's linear,
+// architecture.py:696-700): CTA b takes the rows e = b, b + G, ...; a pass covers
+// two rows and up to RTP tokens; warp w the K-eighth [w D/8, (w+1) D/8) of both
+// rows.  bf16 products are exact in fp64 and summed in fp64 (lane, then warp
+// shuffle tree, then the eight warps in order), rounded once to fp32.  The gate
+// weights are held in fp64, so each token element is converted once for both
+// rows.  w0: the chunk of pass 0, loaded by the caller (before the launch's
+// wait for the previous kernel: the gate weights do not depend on it).
+// SMEM: the tokens are staged in shared memory at xsm (else read from a.x).
+template <int RTP, bool SMEM>
+__device__ void router_logits_t(const MoeArgs &a, const Smem &sm, const __nv_bfloat16 *xsm, const GateChunk &w0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = a.E, D = a.D, T = a.T;
     const int G = gridDim.x;
-    static_assert(2 * 4 * RTP * 8 <= MISC_BYTES, "router partials must fit the misc buffer");
-    double *part = sm.misc();  // [2 rows][4 parts][RTP tokens]
+    static_assert(2 * NCW * RTP * 8 <= MISC_BYTES, "router partials must fit the misc buffer");
+    double *part = sm.misc();  // [2 rows][NCW warps][RTP tokens]
     const int nrows = (blockIdx.x < E) ? cdiv(E - blockIdx.x, G) : 0;
-    const int quarter = D / 4;
+    const int eighth = D / 8;
     for (int p = 0; p < nrows; p += 2) {
-        const int rl = warp >> 2, pq = warp & 3;
-        const int r = p + rl;
-        const bool rv = r < nrows;
-        const int e = blockIdx.x + r * G;
-        const __nv_bfloat16 *wrow = a.gate_w + (size_t)(rv ? e : 0) * D + pq * quarter;
-        // every load of a pass is issued before the first use: one memory
-        // latency per pass (the kernel's critical path is latency, not bytes)
-        float wf[KU][8];
+        double wd[2][RKE][8];
         {
-            uint4 wu[KU];
+            const GateChunk wc = p == 0 ? w0 : load_gate_chunk(a, p);
 #pragma unroll
-            for (int u = 0; u < KU; ++u) {
-                const int k = lane * 8 + u * 256;
-                wu[u] = (rv && k < quarter) ? ldg128(wrow + k) : make_uint4(0, 0, 0, 0);
-            }
+            for (int rl = 0; rl < 2; ++rl)
 #pragma unroll
-            for (int u = 0; u < KU; ++u) {
-                const uint32_t wv[4] = {wu[u].x, wu[u].y, wu[u].z, wu[u].w};
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    wf[u][2 * c] = bf16_bits_to_f32(wv[c] & 0xffffu);
-                    wf[u][2 * c + 1] = bf16_bits_to_f32(wv[c] >> 16);
-                }
-            }
-        }
-        for (int t0 = 0; t0 < T; t0 += RTP) {
-            uint4 xu[KU][RTP];
-#pragma unroll
-            for (int u = 0; u < KU; ++u)
-#pragma unroll
-                for (int t = 0; t < RTP; ++t) {
-                    const int k = lane * 8 + u * 256;
-                    const size_t off = (size_t)(t0 + t) * D + pq * quarter + k;
-                    xu[u][t] = (rv && k < quarter && t0 + t < T)
-                                   ? (xsm ? lds128(xsm + off) : ldg128(a.x + off))
-                                   : make_uint4(0, 0, 0, 0);
-                }
-            double accd[RTP];
-#pragma unroll
-            for (int t = 0; t < RTP; ++t) {
-                accd[t] = 0.0;
-#pragma unroll
-                for (int u = 0; u < KU; ++u) {
-                    const uint32_t xv[4] = {xu[u][t].x, xu[u][t].y, xu[u][t].z, xu[u][t].w};
-                    double s = 0.0;
+                for (int u = 0; u < RKE; ++u) {
+                    const uint32_t wv[4] = {wc.w[rl][u].x, wc.w[rl][u].y, wc.w[rl][u].z, wc.w[rl][u].w};
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        // bf16 x bf16 products are exact in fp32
-                        s += (double)(wf[u][2 * c] * bf16_bits_to_f32(xv[c] & 0xffffu));
-                        s += (double)(wf[u][2 * c + 1] * bf16_bits_to_f32(xv[c] >> 16));
+                        wd[rl][u][2 * c] = (double)bf16_bits_to_f32(wv[c] & 0xffffu);
+                        wd[rl][u][2 * c + 1] = (double)bf16_bits_to_f32(wv[c] >> 16);
                     }
-                    accd[t] += s;
+                }
+        }
+        for (int t0 = 0; t0 < T; t0 += RTP) {
+            const int nt = min(RTP, T - t0);
+            auto load_x = [&](int t, int u) -> uint4 {
+                const int k = lane * 8 + u * 256;
+                const size_t off = (size_t)(t0 + t) * D + warp * eighth + k;
+                return (t < nt && k < eighth) ? (SMEM ? lds128(xsm + off) : ldg128(a.x + off)) : make_uint4(0, 0, 0, 0);
+            };
+            // from global memory every load of the pass is issued before the first
+            // use (one memory latency per pass: the critical path is latency, not
+            // bytes); from shared memory each token's loads come with its math
+            uint4 xg[SMEM ? 1 : RTP][RKE];
+            if (!SMEM) {
+#pragma unroll
+                for (int t = 0; t < (SMEM ? 1 : RTP); ++t)
+#pragma unroll
+                    for (int u = 0; u < RKE; ++u) xg[t][u] = load_x(t, u);
+            }
+            double acc[2][RTP];
+#pragma unroll
+            for (int t = 0; t < RTP; ++t) {
+                acc[0][t] = 0.0;
+                acc[1][t] = 0.0;
+                if (t >= nt) continue;
+#pragma unroll
+                for (int u = 0; u < RKE; ++u) {
+                    const uint4 xq = SMEM ? load_x(t, u) : xg[SMEM ? 0 : t][u];
+                    const uint32_t xv[4] = {xq.x, xq.y, xq.z, xq.w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const double x0 = (double)bf16_bits_to_f32(xv[c] & 0xffffu);
+                        const double x1 = (double)bf16_bits_to_f32(xv[c] >> 16);
+                        acc[0][t] = fma(x0, wd[0][u][2 * c], acc[0][t]);
+                        acc[1][t] = fma(x0, wd[1][u][2 * c], acc[1][t]);
+                        acc[0][t] = fma(x1, wd[0][u][2 * c + 1], acc[0][t]);
+                        acc[1][t] = fma(x1, wd[1][u][2 * c + 1], acc[1][t]);
+                    }
                 }
             }
 #pragma unroll
             for (int t = 0; t < RTP; ++t) {
-                double v = accd[t];
+                if (t >= nt) continue;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                accd[t] = v;
+                for (int rl = 0; rl < 2; ++rl) {
+                    double v = acc[rl][t];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    acc[rl][t] = v;
+                }
             }
             if (lane == 0) {
 #pragma unroll
-                for (int t = 0; t < RTP; ++t) part[(rl * 4 + pq) * RTP + t] = accd[t];
+                for (int t = 0; t < RTP; ++t)
+#pragma unroll
+                    for (int rl = 0; rl < 2; ++rl) part[(rl * NCW + warp) * RTP + t] = acc[rl][t];
             }
             bar_sync(1, NCT);
             if (threadIdx.x < 2 * RTP) {
                 const int rl2 = threadIdx.x / RTP, t = threadIdx.x % RTP;
                 const int r2 = p + rl2;
-                if (r2 < nrows && t0 + t < T) {
-                    const double v = part[(rl2 * 4 + 0) * RTP + t] + part[(rl2 * 4 + 1) * RTP + t] +
-                                     part[(rl2 * 4 + 2) * RTP + t] + part[(rl2 * 4 + 3) * RTP + t];
+                if (r2 < nrows && t < nt) {
+                    double v = 0.0;
+#pragma unroll
+                    for (int w = 0; w < NCW; ++w) v += part[(rl2 * NCW + w) * RTP + t];
                     a.logits[(size_t)(t0 + t) * E + blockIdx.x + r2 * G] = (float)v;
                 }
             }
             bar_sync(1, NCT);
         }
     }
+}
+
+__device__ void router_logits(const MoeArgs &a, const Smem &sm, const __nv_bfloat16 *xsm, const GateChunk &w0) {
+    // tokens in shared memory: eight per pass (loads are cheap, fewer barriers);
+    // from global memory: four, every load of the pass in flight at once
+    if (xsm) router_logits_t<8, true>(a, sm, xsm, w0);
+    else router_logits_t<4, false>(a, sm, xsm, w0);
 }
 
 __device__ __forceinline__ void warp_argmax(float &v, int &idx) {
@@ -955,6 +1004,47 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
     __syncwarp();
 }
 
+// Waits (bounded by `limit` SM cycles) until *ctr >= target, reading it with
+// acquire semantics; on a timeout sets kErrTimeout and returns false.
+__device__ bool wait_count(const unsigned *ctr, unsigned target, int *err, long long limit) {
+    const long long t0 = clock64();
+    while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        if (clock64() - t0 > limit) {
+            atomicOr(err, kErrTimeout);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+// Top-k of more tokens than one CTA has warps: router CTA b < ntk takes the
+// tokens b * NCW + warp (+ ntk * NCW ...), one warp per token, once every router
+// CTA's logits are written, and stores each token's experts and weights in
+// a.ridx / a.rw for the CTA that builds the dispatch tables.
+__device__ void topk_spread(const MoeArgs &a, const Smem &sm, unsigned nrc, unsigned ntk) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = a.topk;
+    int16_t *ridx_s = reinterpret_cast<int16_t *>(sm.red());
+    int16_t *pof_s = ridx_s + MAX_T * MAX_K;
+    float *rw_s = reinterpret_cast<float *>(pof_s + MAX_T * MAX_K);
+    float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);
+    if (threadIdx.x == 0) wait_count(a.cnt_router, nrc, a.err, a.wait_limit);
+    bar_sync(1, NCT);
+    for (int t = (int)blockIdx.x * NCW + warp; t < a.T; t += (int)ntk * NCW) {
+        if (a.E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        if (lane < K) {
+            a.ridx[t * K + lane] = ridx_s[t * K + lane];
+            a.rw[t * K + lane] = rw_s[t * K + lane];
+        }
+    }
+    __threadfence();
+    bar_sync(1, NCT);
+}
+
 // Top-k and dispatch tables; run by the 256 consumer threads of one CTA.
 // Every phase is spread over the block (the router kernel's critical path):
 //   1. top-k per token, one warp per token           -> ridx_s, rw_s, outputs
@@ -963,7 +1053,7 @@ __device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float
 //   3. block scan over local experts                 -> act_* tables, header
 //   4. per kept slot: rank among the expert's tokens (bitmap popcount) -> pair
 //   5. per token: its pairs in ascending expert order -> tok_pairs
-__device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
+__device__ void topk_dispatch(const MoeArgs &a, const Smem &sm, bool spread = false) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int T = a.T, E = a.E, K = a.topk, El = a.El;
     static_assert(MAX_T * MAX_K * (2 + 2 + 4) <= RED_BYTES, "top-k tables must fit the reduction buffer");
@@ -978,13 +1068,14 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
     unsigned long long *scan_ws = reinterpret_cast<unsigned long long *>(off_s + MAX_E);   // [NCW]
     const int TW = (T + 31) >> 5;
     // ---- 1. top-k: one warp per token, scores of the warp's token in shared memory
-    // (routed-only calls take the routing computed by the ranks that own the tokens)
-    if (a.given) {
+    // (routed-only calls take the routing computed by the ranks that own the tokens;
+    // `spread`: the router CTAs computed it, topk_spread, into a.ridx / a.rw)
+    if (a.given || spread) {
         for (int slot = tid; slot < T * K; slot += NCT) {
-            long long e = __ldg(a.in_idx + slot);
+            long long e = a.given ? __ldg(a.in_idx + slot) : (long long)__ldcg(a.ridx + slot);
             if (e < 0 || e >= E) { atomicOr(a.err, kErrExpertId); e = 0; }
             ridx_s[slot] = (int16_t)e;
-            rw_s[slot] = __ldg(a.in_w + slot);
+            rw_s[slot] = a.given ? __ldg(a.in_w + slot) : __ldcg(a.rw + slot);
             pof_s[slot] = -1;
         }
     } else {
@@ -1050,9 +1141,16 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
         a.hdr[H_NPAIR] = off;
     }
     bar_sync(1, NCT);
-    // ---- 4. pairs: expert ascending, token ascending within an expert
+    // ---- 4. pairs: expert ascending, token ascending within an expert.  On the
+    // tcgen05 engine each slot's expert and pair (-1: none) go to a.ridx and
+    // a.tok_pairs, and the w2 kernel builds the per-token lists of step 5 in its
+    // prologue, while the w1/w3 kernel runs.
     for (int slot = tid; slot < T * K; slot += NCT) {
-        if (pof_s[slot] != -2) continue;
+        if (a.tc) a.ridx[slot] = ridx_s[slot];
+        if (pof_s[slot] != -2) {
+            if (a.tc) a.tok_pairs[slot] = -1;
+            continue;
+        }
         const int t = slot / K;
         const int el = ridx_s[slot] - a.e0;
         const uint32_t *row = bm + el * TW;
@@ -1062,6 +1160,11 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm) {
         a.pair_tok[p] = t;
         a.pair_w[p] = rw_s[slot];
         pof_s[slot] = (int16_t)p;
+        if (a.tc) a.tok_pairs[slot] = p;
+    }
+    if (a.tc) {
+        __threadfence();
+        return;
     }
     bar_sync(1, NCT);
     // ---- 5. each token's pairs in ascending expert order (a token's kept experts
@@ -1268,6 +1371,9 @@ __device__ void quantize_tokens_warp(const MoeArgs &a) {
 __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem sm{smem_raw};
+    // the first pass's gate rows do not depend on the previous kernel
+    GateChunk w0{};
+    if (!a.given && (threadIdx.x >> 5) < NCW) w0 = load_gate_chunk(a, 0);
     init_smem(sm);
     pdl_wait();
     pdl_launch_dependents();
@@ -1309,20 +1415,35 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
     } else {
     const __nv_bfloat16 *xsm = nullptr;
     if (stage_x && wf_wait(sm.full(0), 0, a.err)) xsm = reinterpret_cast<const __nv_bfloat16 *>(sm.slot(0));
-    router_logits(a, sm, xsm);
+    router_logits(a, sm, xsm, w0);
     __threadfence();
     bar_sync(1, NCT);
     const unsigned nrc = min((unsigned)a.E, gridDim.x);
     if (blockIdx.x < nrc) {
+        // More tokens than warps: the top-k runs on the first ntk router CTAs, one
+        // warp per token, and the last of them to finish builds the tables.
+        // Otherwise the last router CTA to arrive does both.
+        const bool spread = a.T > NCW;
+        const unsigned ntk = spread ? min(nrc, (unsigned)cdiv(a.T, NCW)) : 1u;
         if (threadIdx.x == 0) {
             const unsigned old = atomicAdd(a.cnt_router, 1u);
-            sm.flags()[1] = (old == nrc - 1);
+            sm.flags()[1] = spread ? (blockIdx.x < ntk) : (old == nrc - 1);
         }
         bar_sync(1, NCT);
         if (sm.flags()[1]) {
-            __threadfence();
-            topk_dispatch(a, sm);
-            if (threadIdx.x == 0) *a.cnt_router = 0u;
+            if (spread) {
+                topk_spread(a, sm, nrc, ntk);
+                if (threadIdx.x == 0) {
+                    const unsigned old = atomicAdd(a.cnt_router + 1, 1u);
+                    sm.flags()[1] = (old == ntk - 1);
+                }
+                bar_sync(1, NCT);
+            }
+            if (!spread || sm.flags()[1]) {
+                __threadfence();
+                topk_dispatch(a, sm, spread);
+                if (threadIdx.x == 0) { a.cnt_router[0] = 0u; a.cnt_router[1] = 0u; }
+            }
         }
         bar_sync(1, NCT);
     }

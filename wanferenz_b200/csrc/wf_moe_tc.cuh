@@ -67,6 +67,7 @@ constexpr int SMEM = OFF_TOK + TOK_BYTES + 1024;  // + alignment slack
 static_assert(MAX_PAIRS <= 32767, "pair indices fit int16");
 static_assert(SMEM <= 232448, "shared memory budget");
 static_assert(OFF_EX % 16 == 0 && (AM_LD * 4) % 16 == 0, "float4 rows of the amax tile");
+static_assert(2 * MAX_T * MAX_K * 2 <= EX_BYTES, "the w2 phase stages per-slot routing in the amax tile");
 // TMEM columns (512 allocated)
 constexpr uint32_t COL_D = 0;      // [issuer][buf][tile] x NT
 constexpr uint32_t COL_SFB = 192;  // [K step] x 4
@@ -217,17 +218,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         fence_mbar_init();
     }
     if (warp == W_PROD) { tc::tmem_alloc(tmem_slot, 512); tc::tmem_relinquish(); }
-    // everything below reads what the previous kernel wrote
-    pdl_wait();
-    pdl_launch_dependents();
-    const int n_act = a.hdr[H_NACT];
+    // The w1/w3 phase reads the router kernel's tables: everything waits for it.
+    // The w2 phase reads the same tables, and the router kernel completed before
+    // the w1/w3 kernel passed its own wait (which precedes its launch of this
+    // one), so they are read here at once, through L2; the producer then fills
+    // the weight ring while the w1/w3 kernel finishes.  Only the worker warps,
+    // which read its outputs (h, the shared hidden rows, their scales), wait.
+    if (PH == 2) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
+    // the header and every table entry the workspace holds, in one round trip
+    // (entries past n_act are never used)
+    const int n_act = __ldcg(a.hdr + H_NACT);
+    const int n_rt = __ldcg(a.hdr + (PH == 2 ? H_IT2 : H_IT3));
     TRoute r;
     {
         const int *src_it = PH == 2 ? a.act_it2 : a.act_it3;
-        for (int k = threadIdx.x; k <= n_act; k += THREADS) {
-            rt_s[k] = k < n_act ? a.act_expert[k] : 0;
-            rt_s[(MAX_E + 1) + k] = a.act_off[k];
-            rt_s[2 * (MAX_E + 1) + k] = src_it[k];
+        for (int k = threadIdx.x; k <= a.El; k += THREADS) {
+            const int ve = __ldcg(a.act_expert + k), vo = __ldcg(a.act_off + k), vi = __ldcg(src_it + k);
+            rt_s[k] = ve;
+            rt_s[(MAX_E + 1) + k] = vo;
+            rt_s[2 * (MAX_E + 1) + k] = vi;
         }
         r.act_expert = rt_s;
         r.act_off = rt_s + (MAX_E + 1);
@@ -236,9 +248,33 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
         r.nblk = PH == 2 ? a.I / 128 : a.D / 256;
         r.ns = r.nblk * cdiv(a.shT, NT);  // shared items
         if (PH == 3) {
-            // the combine's pair lists (written by the router kernel)
-            for (int k = threadIdx.x; k < a.T * a.topk; k += THREADS) tp_s[k] = (int16_t)__ldcg(a.tok_pairs + k);
-            for (int k = threadIdx.x; k < a.T; k += THREADS) np_s[k] = (uint8_t)__ldcg(a.tok_np + k);
+            // The combine's lists: each token's pairs in ascending expert order
+            // (a token's kept experts are distinct, so a slot's place is the number
+            // of its kept slots with a smaller expert), from the router kernel's
+            // per-slot expert (a.ridx) and pair (a.tok_pairs, -1: none), staged in
+            // the amax tile, which this phase does not use.
+            const int TK = a.T * a.topk, K = a.topk;
+            int16_t *sr = reinterpret_cast<int16_t *>(ex);
+            int16_t *sp = sr + MAX_T * MAX_K;
+            for (int k = threadIdx.x; k < TK; k += THREADS) {
+                const int e = __ldcg(a.ridx + k), pr = __ldcg(a.tok_pairs + k);
+                sr[k] = (int16_t)e;
+                sp[k] = (int16_t)pr;
+            }
+            __syncthreads();
+            for (int t = threadIdx.x; t < a.T; t += THREADS) {
+                int n = 0;
+                for (int j = 0; j < K; ++j) {
+                    const int pr = sp[t * K + j];
+                    if (pr < 0) continue;
+                    const int e = sr[t * K + j];
+                    int rank = 0;
+                    for (int j2 = 0; j2 < K; ++j2) rank += (sp[t * K + j2] >= 0 && sr[t * K + j2] < e) ? 1 : 0;
+                    tp_s[t * K + rank] = (int16_t)pr;
+                    ++n;
+                }
+                np_s[t] = (uint8_t)n;
+            }
         }
     }
     tc::fence_before_sync();
@@ -252,7 +288,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     // stages: what the B operand leaves of the shared region
     const int nstg = min(MAX_STAGES, (AB_BYTES - nst * BSTEP) / STAGE_BYTES);
     uint8_t *const Bbase = base + OFF_A + nstg * STAGE_BYTES;
-    const int n_items = r.ns + (PH == 2 ? a.hdr[H_IT2] : a.hdr[H_IT3]);
+    const int n_items = r.ns + n_rt;
     const long long S = (long long)n_items * nst;
     // the CTAs that share the S steps (the others have none)
     const int G = (int)max(1LL, min((long long)gridDim.x, S / MIN_SEG));
@@ -260,6 +296,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
     if (PH == 3 && n_items == 0 && warp < 4) {
         // no item at all (a routed-only call whose shard got no tokens): the combine
         // still writes every row block (zeros)
+        pdl_wait();
+        pdl_launch_dependents();
         for (int rb = blockIdx.x; rb < D / 256; rb += gridDim.x) combine_rows_v8<NWK>(a, rb * 256, 256, np_s, tp_s);
     }
     // segment after `sg` (or the first one when sg.q < 0); false at the end of the range
@@ -558,6 +596,84 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
             }
         };
 
+        // Weight scale factors of K steps [g0, end of g0's aligned group of GRP, cut
+        // at j1) of item `it` into TMEM slot gi & 1 for the issuers; returns the
+        // group's end, or -1 when a wait ran out.  They depend on the weights only.
+        auto sfa_group = [&](const TItem &it, int g0, int j1) -> int {
+            const int g1 = min((g0 & ~(GRP - 1)) + GRP, j1);
+            const int ga = g0 & ~(GRP - 1);  // first step of the aligned group
+            // global loads first; the wait below only guards the TMEM slot
+            uint32_t w[GRP][2][4];
+            if (it.shared) {
+                const uint8_t *s8 = (const uint8_t *)(PH == 2 ? a.ss13 : a.ss2);
+                const int kb = K / 128;
+#pragma unroll
+                for (int jj = 0; jj < GRP; ++jj)
+#pragma unroll
+                    for (int tt = 0; tt < 2; ++tt) {
+                        const int rb = PH == 2 ? tt * (I / 128) + it.blk : 2 * it.blk + tt;
+                        const uint32_t v = (ga + jj >= g0 && ga + jj < g1)
+                                               ? 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + ga + jj)
+                                               : 0x7f7f7f7fu;
+                        w[jj][tt][0] = w[jj][tt][1] = w[jj][tt][2] = w[jj][tt][3] = v;
+                    }
+            } else {
+                const int ks = K / 32;
+                const uint8_t *sb = PH == 2 ? a.w13_s + (size_t)it.el * (2 * I) * ks
+                                            : a.w2_s + (size_t)it.el * D * ks;
+#pragma unroll
+                for (int tt = 0; tt < 2; ++tt)
+#pragma unroll
+                    for (int r1 = 0; r1 < 4; ++r1) {
+                        const int rr = 32 * r1 + lane;
+                        const int grow = PH == 2 ? tt * I + it.blk * 128 + rr : it.blk * 256 + tt * 128 + rr;
+                        const uint8_t *src = sb + (size_t)grow * ks + (size_t)ga * 4;
+                        if ((nst & (GRP - 1)) == 0) {
+                            // the row's 8 words of this group: two 16-byte loads
+                            const uint4 lo = ldg128(src), hi = ldg128(src + 16);
+                            w[0][tt][r1] = lo.x; w[1][tt][r1] = lo.y; w[2][tt][r1] = lo.z; w[3][tt][r1] = lo.w;
+                            w[4][tt][r1] = hi.x; w[5][tt][r1] = hi.y; w[6][tt][r1] = hi.z; w[7][tt][r1] = hi.w;
+                        } else {
+#pragma unroll
+                            for (int jj = 0; jj < GRP; ++jj)
+                                w[jj][tt][r1] = (ga + jj >= g0 && ga + jj < g1)
+                                                    ? __ldg(reinterpret_cast<const uint32_t *>(src) + jj)
+                                                    : 0x7f7f7f7fu;
+                        }
+                    }
+            }
+            if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) return -1;
+            tc::fence_after_sync();
+            const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
+#pragma unroll
+            for (int jj = 0; jj < GRP; ++jj)
+                if (ga + jj >= g0 && ga + jj < g1) {
+#pragma unroll
+                    for (int tt = 0; tt < 2; ++tt)
+                        tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
+                                     w[jj][tt][2], w[jj][tt][3]);
+                }
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(B.sfa_ready + (gi & 1));
+            ++gi;
+            return g1;
+        };
+        // The first group of the CTA's first segment is staged before its B operand
+        // and, in the w2 phase, before the wait for the w1/w3 kernel, whose outputs
+        // the B operand is: the first MMA then starts as soon as B is in place.
+        int g_pre = -1;
+        {
+            Seg s0{0, 0, 0, -1};
+            TCursor c0;
+            if (next_seg(s0)) g_pre = sfa_group(decode<PH>(a, r, c0, s0.i), s0.j0, s0.j1);
+        }
+        if (PH == 3) {
+            pdl_wait();
+            pdl_launch_dependents();
+        }
+
         Seg prev{0, 0, 0, -1};
         bool have_prev = false;
         while (!dead && next_seg(sg)) {
@@ -612,67 +728,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
                 key = it.key;
             }
             // weight scale factors by groups of K steps [8k, 8k+8) cut to the segment;
-            // the previous segment's epilogue runs once two groups are queued
+            // the previous segment's epilogue runs once two groups are queued (the
+            // first segment's first group went ahead of its B operand)
             int ngrp = 0;
-            for (int g0 = sg.j0; g0 < sg.j1 && !dead;) {
-                const int g1 = min((g0 & ~(GRP - 1)) + GRP, sg.j1);
-                const int ga = g0 & ~(GRP - 1);  // first step of the aligned group
-                // global loads first; the wait below only guards the TMEM slot
-                uint32_t w[GRP][2][4];
-                if (it.shared) {
-                    const uint8_t *s8 = (const uint8_t *)(PH == 2 ? a.ss13 : a.ss2);
-                    const int kb = K / 128;
-#pragma unroll
-                    for (int jj = 0; jj < GRP; ++jj)
-#pragma unroll
-                        for (int tt = 0; tt < 2; ++tt) {
-                            const int rb = PH == 2 ? tt * (I / 128) + it.blk : 2 * it.blk + tt;
-                            const uint32_t v = (ga + jj >= g0 && ga + jj < g1)
-                                                   ? 0x01010101u * (uint32_t)__ldg(s8 + (size_t)rb * kb + ga + jj)
-                                                   : 0x7f7f7f7fu;
-                            w[jj][tt][0] = w[jj][tt][1] = w[jj][tt][2] = w[jj][tt][3] = v;
-                        }
-                } else {
-                    const int ks = K / 32;
-                    const uint8_t *sb = PH == 2 ? a.w13_s + (size_t)it.el * (2 * I) * ks
-                                                : a.w2_s + (size_t)it.el * D * ks;
-#pragma unroll
-                    for (int tt = 0; tt < 2; ++tt)
-#pragma unroll
-                        for (int r1 = 0; r1 < 4; ++r1) {
-                            const int rr = 32 * r1 + lane;
-                            const int grow = PH == 2 ? tt * I + it.blk * 128 + rr : it.blk * 256 + tt * 128 + rr;
-                            const uint8_t *src = sb + (size_t)grow * ks + (size_t)ga * 4;
-                            if ((nst & (GRP - 1)) == 0) {
-                                // the row's 8 words of this group: two 16-byte loads
-                                const uint4 lo = ldg128(src), hi = ldg128(src + 16);
-                                w[0][tt][r1] = lo.x; w[1][tt][r1] = lo.y; w[2][tt][r1] = lo.z; w[3][tt][r1] = lo.w;
-                                w[4][tt][r1] = hi.x; w[5][tt][r1] = hi.y; w[6][tt][r1] = hi.z; w[7][tt][r1] = hi.w;
-                            } else {
-#pragma unroll
-                                for (int jj = 0; jj < GRP; ++jj)
-                                    w[jj][tt][r1] = (ga + jj >= g0 && ga + jj < g1)
-                                                        ? __ldg(reinterpret_cast<const uint32_t *>(src) + jj)
-                                                        : 0x7f7f7f7fu;
-                            }
-                        }
-                }
-                if (gi >= 2 && !wwait(B.sfa_free + (gi & 1), ((gi >> 1) - 1) & 1)) break;
-                tc::fence_after_sync();
-                const uint32_t cbase = tm + lane_base + COL_SFA + (uint32_t)((gi & 1) * (GRP * 8));
-#pragma unroll
-                for (int jj = 0; jj < GRP; ++jj)
-                    if (ga + jj >= g0 && ga + jj < g1) {
-#pragma unroll
-                        for (int tt = 0; tt < 2; ++tt)
-                            tc::tmem_st4(cbase + (uint32_t)((jj * 2 + tt) * 4), w[jj][tt][0], w[jj][tt][1],
-                                         w[jj][tt][2], w[jj][tt][3]);
-                    }
-                tc::tmem_wait_st();
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(B.sfa_ready + (gi & 1));
-                ++gi;
+            for (int g0 = (sg.q == 0 && g_pre > 0) ? g_pre : sg.j0; g0 < sg.j1 && !dead;) {
+                const int g1 = sfa_group(it, g0, sg.j1);
+                if (g1 < 0) break;
                 ++ngrp;
                 g0 = g1;
                 if (have_prev && (ngrp == 2 || (ngrp == 1 && g1 == sg.j1))) epilogue(prev);
