@@ -660,14 +660,31 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_tc(const __grid_constant__ M
             ++gi;
             return g1;
         };
-        // The first group of the CTA's first segment is staged before its B operand
-        // and, in the w2 phase, before the wait for the w1/w3 kernel, whose outputs
-        // the B operand is: the first MMA then starts as soon as B is in place.
+        // The w2 phase stages the first group of the CTA's first segment before the
+        // wait for the w1/w3 kernel, whose outputs its B operand is: the first MMA
+        // then starts as soon as B is in place.  The w1/w3 phase cannot start before
+        // its wait (the item comes from the routing); it sends the group's scale
+        // rows towards L2 and loads B, whose latency the prefetch then hides.
         int g_pre = -1;
         {
             Seg s0{0, 0, 0, -1};
             TCursor c0;
-            if (next_seg(s0)) g_pre = sfa_group(decode<PH>(a, r, c0, s0.i), s0.j0, s0.j1);
+            if (next_seg(s0)) {
+                const TItem it0 = decode<PH>(a, r, c0, s0.i);
+                if (PH == 3) {
+                    g_pre = sfa_group(it0, s0.j0, s0.j1);
+                } else if (!it0.shared) {
+                    const int ks = K / 32, ga = s0.j0 & ~(GRP - 1);
+                    const uint8_t *sb = a.w13_s + (size_t)it0.el * (2 * I) * ks;
+#pragma unroll
+                    for (int tt = 0; tt < 2; ++tt)
+#pragma unroll
+                        for (int r1 = 0; r1 < 4; ++r1) {
+                            const int grow = tt * I + it0.blk * 128 + 32 * r1 + lane;
+                            asm volatile("prefetch.global.L2 [%0];" ::"l"(sb + (size_t)grow * ks + (size_t)ga * 4));
+                        }
+                }
+            }
         }
         if (PH == 3) {
             pdl_wait();
