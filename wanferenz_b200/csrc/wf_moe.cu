@@ -889,10 +889,35 @@ __device__ __forceinline__ unsigned long long block_scan_u64(unsigned long long 
 // dry: a warm-up pass on whatever the logits hold (shared-memory outputs only,
 // no global writes, no error reports) that loads this code into the SM's
 // instruction cache before the real pass runs on the last router CTA.
+// The routing inputs of topk_token, passed by value: inside the non-inlined
+// function the kernel's argument block would be read through a pointer, one
+// dependent load per field on a cold SM.
+struct TopkIn {
+    const float *logits;
+    const float *gate_b;
+    const long long *ids;
+    const int *tid2eid;
+    float *out_w;
+    long long *out_idx;
+    int *err;
+    int E, K, score_func, hash;
+    long long vocab;
+    float route_scale;
+};
+
+__device__ __forceinline__ TopkIn topk_in(const MoeArgs &a) {
+    TopkIn q;
+    q.logits = a.logits; q.gate_b = a.gate_b; q.ids = a.ids; q.tid2eid = a.tid2eid;
+    q.out_w = a.out_w; q.out_idx = a.out_idx; q.err = a.err;
+    q.E = a.E; q.K = a.topk; q.score_func = a.score_func; q.hash = a.hash; q.vocab = a.vocab;
+    q.route_scale = a.route_scale;
+    return q;
+}
+
 template <int NE>
-__device__ __noinline__ void topk_token(const MoeArgs &a, int t, int lane, float *sc_w, int16_t *ridx_s,
+__device__ __noinline__ void topk_token(const TopkIn a, int t, int lane, float *sc_w, int16_t *ridx_s,
                                         int16_t *pof_s, float *rw_s, bool dry) {
-    const int E = a.E, K = a.topk;
+    const int E = a.E, K = a.K;
     float sc[NE], bs[NE], gb[NE];
     // logits and gate bias in one round trip
 #pragma unroll
@@ -1034,8 +1059,8 @@ __device__ void topk_spread(const MoeArgs &a, const Smem &sm, unsigned nrc, unsi
     if (threadIdx.x == 0) wait_count(a.cnt_router, nrc, a.err, a.wait_limit);
     bar_sync(1, NCT);
     for (int t = (int)blockIdx.x * NCW + warp; t < a.T; t += (int)ntk * NCW) {
-        if (a.E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
-        else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        if (a.E <= 256) topk_token<8>(topk_in(a), t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+        else topk_token<MAX_E / 32>(topk_in(a), t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
         if (lane < K) {
             a.ridx[t * K + lane] = ridx_s[t * K + lane];
             a.rw[t * K + lane] = rw_s[t * K + lane];
@@ -1081,8 +1106,8 @@ __device__ void topk_dispatch(const MoeArgs &a, const Smem &sm, bool spread = fa
     } else {
         float *sc_all = reinterpret_cast<float *>(sm.base + OFF_ROUTE);  // [NCW][MAX_E]
         for (int t = warp; t < T; t += NCW) {
-            if (E <= 256) topk_token<8>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
-            else topk_token<MAX_E / 32>(a, t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+            if (E <= 256) topk_token<8>(topk_in(a), t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
+            else topk_token<MAX_E / 32>(topk_in(a), t, lane, sc_all + warp * MAX_E, ridx_s, pof_s, rw_s, false);
         }
     }
     bar_sync(1, NCT);
@@ -1401,8 +1426,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_moe_up(const __grid_constant__ MoeA
                 int16_t *ri = reinterpret_cast<int16_t *>(scratch + 4 * MAX_E);        // [MAX_K]
                 int16_t *po = ri + MAX_K;                                              // [MAX_K]
                 float *rw = reinterpret_cast<float *>(po + MAX_K);                     // [MAX_K]
-                if (a.E <= 256) topk_token<8>(a, 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
-                else topk_token<MAX_E / 32>(a, 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
+                if (a.E <= 256) topk_token<8>(topk_in(a), 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
+                else topk_token<MAX_E / 32>(topk_in(a), 0, threadIdx.x & 31, sc_w, ri, po, rw, true);
             }
             return;
         }

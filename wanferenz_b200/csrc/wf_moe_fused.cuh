@@ -792,8 +792,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_fused(const __grid_constant_
             float *rw_s = reinterpret_cast<float *>(scr + R_RW);
             const int Tq = a.ep ? a.Tr : a.T;
             for (int tk = blockIdx.x + warp * G; tk < Tq; tk += 4 * G) {
-                if (a.E <= 256) topk_token<8>(a, tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
-                else topk_token<MAX_E / 32>(a, tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
+                if (a.E <= 256) topk_token<8>(topk_in(a), tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
+                else topk_token<MAX_E / 32>(topk_in(a), tk, lane, sc_w, ridx_s, pof_s, rw_s, false);
                 if (lane < a.topk) {
                     const int e = ridx_s[tk * a.topk + lane];
                     const float w = rw_s[tk * a.topk + lane];
