@@ -615,6 +615,8 @@ def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter", peers=(
     import torch
     import torch.distributed as dist
 
+    if world > 1:
+        return run_e2e_graphs(layers, T, K, W, dev, world, combine, peers)
     n = K + W
     xh = [torch.randn(T, D).to(torch.bfloat16).pin_memory() for _ in range(n)]
     yh = [torch.empty(T, D, dtype=torch.bfloat16).pin_memory() for _ in range(n)]
@@ -681,6 +683,98 @@ def run_e2e(layers, T, K, W, dev, world, rank, combine="reduce_scatter", peers=(
             "d2h_bytes_per_step": T * D * 2, "copies": "own stream, overlapped with compute",
             "api": ("wanferenz_b200.moe.MoELayer.forward" if world == 1 else
                     "wanferenz_b200.ep.PeerGroup.forward" if peers else "wanferenz_b200.ep.ep_forward")}
+
+
+def run_e2e_graphs(layers, T, K, W, dev, world, combine="reduce_scatter", peers=()):
+    """run_e2e for N > 1 ranks: each layer's public call (``ep.ep_forward`` or
+    ``PeerGroup.forward``, exchange included) is captured once in a CUDA graph, as a
+    serving loop would, and replayed every step; the host copies stay outside the
+    graphs, on their own stream, overlapping the previous step's compute.  Every
+    rank captures and replays the same sequence."""
+    import torch
+    import torch.distributed as dist
+
+    n = K + W
+    nl = len(layers)
+    xh = [torch.randn(T, D).to(torch.bfloat16).pin_memory() for _ in range(n)]
+    yh = [torch.empty(T, D, dtype=torch.bfloat16).pin_memory() for _ in range(n)]
+    xin = [torch.empty(T, D, dtype=torch.bfloat16, device=dev) for _ in range(nl)]
+
+    def fwd(l):
+        if peers:
+            return peers[l].forward(xin[l])
+        from wanferenz_b200.ep import ep_forward
+        return ep_forward(layers[l], xin[l], combine=combine)
+
+    for l in range(nl):  # eager first: lazy initialisation stays out of the capture
+        fwd(l)
+    torch.cuda.synchronize()
+    graphs, yout = [], []
+    for l in range(nl):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            yout.append(fwd(l))
+        graphs.append(g)
+    torch.cuda.synchronize()
+    main = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    x_in = [torch.cuda.Event() for _ in range(nl)]
+    x_free = [torch.cuda.Event() for _ in range(nl)]
+    y_ok = [torch.cuda.Event() for _ in range(nl)]
+    y_free = [torch.cuda.Event() for _ in range(nl)]
+    used = [False] * nl
+
+    def h2d(i):
+        l = i % nl
+        with torch.cuda.stream(cs):
+            if used[l]:
+                cs.wait_event(x_free[l])
+            xin[l].copy_(xh[i], non_blocking=True)
+            x_in[l].record(cs)
+
+    def one(i, prefetch=True):
+        l = i % nl
+        main.wait_event(x_in[l])
+        if used[l]:
+            main.wait_event(y_free[l])  # the previous output copy of this graph is done
+        graphs[l].replay()
+        used[l] = True
+        x_free[l].record(main)
+        y_ok[l].record(main)
+        if prefetch and i + 1 < n:
+            h2d(i + 1)
+        with torch.cuda.stream(cs):
+            cs.wait_event(y_ok[l])
+            yh[i].copy_(yout[l], non_blocking=True)
+            y_free[l].record(cs)
+
+    h2d(0)
+    for i in range(W):
+        one(i, prefetch=i + 1 < W)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    done = torch.cuda.Event()
+    t0.record(main)
+    cs.wait_event(t0)
+    h2d(W)
+    for i in range(W, n):
+        one(i)
+    done.record(cs)
+    main.wait_event(done)
+    t1.record(main)
+    torch.cuda.synchronize()
+    ms = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item()) / K
+    del graphs, yout  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
+    return {"value": round(T * world / (ms * 1e-3), 1), "unit": "tokens/s",
+            "us_per_step": round(ms * 1e3, 2), "h2d_bytes_per_step": T * D * 2,
+            "d2h_bytes_per_step": T * D * 2,
+            "copies": "own stream, overlapped with compute; each layer's call replayed from a CUDA graph",
+            "api": "wanferenz_b200.ep.PeerGroup.forward" if peers else "wanferenz_b200.ep.ep_forward"}
 
 
 # ---------------------------------------------------------------------------
