@@ -258,7 +258,7 @@ def kernel_names():
 
 # ncu traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the tcgen05
 # expert phases, 16 tokens, uniform routing: profiles/moe_layer_launches_config2_T16.md
-MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 728.9e6, "k_moe_tc<3>": 366.5e6}
+MEASURED_TRAFFIC_T16 = {"k_moe_tc<2>": 728.0e6, "k_moe_tc<3>": 366.2e6}
 
 
 def step_bytes(indices, T, e0, El, router=True, shared=True):
