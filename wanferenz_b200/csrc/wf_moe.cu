@@ -788,25 +788,72 @@ __device__ void router_logits_t(const MoeArgs &a, const Smem &sm, const __nv_bfl
                     for (int u = 0; u < RKE; ++u) xg[t][u] = load_x(t, u);
             }
             double acc[2][RTP];
+            if constexpr (RTP >= 8) {
+                // eight staged tokens: each token's two row chains in turn (measured
+                // faster here than interleaving all sixteen)
 #pragma unroll
-            for (int t = 0; t < RTP; ++t) {
-                acc[0][t] = 0.0;
-                acc[1][t] = 0.0;
-                if (t >= nt) continue;
+                for (int t = 0; t < RTP; ++t) {
+                    acc[0][t] = 0.0;
+                    acc[1][t] = 0.0;
+                    if (t >= nt) continue;
 #pragma unroll
-                for (int u = 0; u < RKE; ++u) {
-                    const uint4 xq = SMEM ? load_x(t, u) : xg[SMEM ? 0 : t][u];
-                    const uint32_t xv[4] = {xq.x, xq.y, xq.z, xq.w};
+                    for (int u = 0; u < RKE; ++u) {
+                        const uint4 xq = SMEM ? load_x(t, u) : xg[SMEM ? 0 : t][u];
+                        const uint32_t xv[4] = {xq.x, xq.y, xq.z, xq.w};
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const double x0 = (double)bf16_bits_to_f32(xv[c] & 0xffffu);
-                        const double x1 = (double)bf16_bits_to_f32(xv[c] >> 16);
-                        acc[0][t] = fma(x0, wd[0][u][2 * c], acc[0][t]);
-                        acc[1][t] = fma(x0, wd[1][u][2 * c], acc[1][t]);
-                        acc[0][t] = fma(x1, wd[0][u][2 * c + 1], acc[0][t]);
-                        acc[1][t] = fma(x1, wd[1][u][2 * c + 1], acc[1][t]);
+                        for (int c = 0; c < 4; ++c) {
+                            const double x0 = (double)bf16_bits_to_f32(xv[c] & 0xffffu);
+                            const double x1 = (double)bf16_bits_to_f32(xv[c] >> 16);
+                            acc[0][t] = fma(x0, wd[0][u][2 * c], acc[0][t]);
+                            acc[1][t] = fma(x0, wd[1][u][2 * c], acc[1][t]);
+                            acc[0][t] = fma(x1, wd[0][u][2 * c + 1], acc[0][t]);
+                            acc[1][t] = fma(x1, wd[1][u][2 * c + 1], acc[1][t]);
+                        }
                     }
                 }
+            } else {
+                // four tokens from global memory: 16 independent fp64 chains per lane, NS sub-sums
+                // for each of the two rows and RTP tokens (element e of the lane's
+                // chunk goes to sub-sum e % NS), added in order at the end; masked
+                // tokens multiply zeros
+                constexpr int NS = 8 / RTP;
+                double acc3[2][RTP][NS];
+#pragma unroll
+                for (int rl = 0; rl < 2; ++rl)
+#pragma unroll
+                    for (int t = 0; t < RTP; ++t)
+#pragma unroll
+                        for (int q = 0; q < NS; ++q) acc3[rl][t][q] = 0.0;
+#pragma unroll
+                for (int u = 0; u < RKE; ++u) {
+                    uint32_t xv[RTP][4];
+#pragma unroll
+                    for (int t = 0; t < RTP; ++t) {
+                        const uint4 xq = SMEM ? load_x(t, u) : xg[SMEM ? 0 : t][u];
+                        xv[t][0] = xq.x; xv[t][1] = xq.y; xv[t][2] = xq.z; xv[t][3] = xq.w;
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            const int q = ((u * 4 + c) * 2 + hh) % NS;
+#pragma unroll
+                            for (int t = 0; t < RTP; ++t) {
+                                const double xd = (double)bf16_bits_to_f32(hh ? (xv[t][c] >> 16) : (xv[t][c] & 0xffffu));
+                                acc3[0][t][q] = fma(xd, wd[0][u][2 * c + hh], acc3[0][t][q]);
+                                acc3[1][t][q] = fma(xd, wd[1][u][2 * c + hh], acc3[1][t][q]);
+                            }
+                        }
+                }
+#pragma unroll
+                for (int rl = 0; rl < 2; ++rl)
+#pragma unroll
+                    for (int t = 0; t < RTP; ++t) {
+                        double v = acc3[rl][t][0];
+#pragma unroll
+                        for (int q = 1; q < NS; ++q) v += acc3[rl][t][q];
+                        acc[rl][t] = v;
+                    }
             }
 #pragma unroll
             for (int t = 0; t < RTP; ++t) {
